@@ -42,6 +42,53 @@ const char* vela_version(void);
 /* GroupNorm statistics of one (sample, group); layout of struct GnStat (src/kernels.h:9). */
 typedef struct vela_gnstat { int64_t sum; int32_t mn, mx; int64_t mean; int32_t e; int32_t pad_; int64_t ss; int64_t sd; } vela_gnstat;
 
+/* Read (and with clear != 0 reset) the device error words of the current device: non-zero when a
+ * bounded wait inside a kernel gave up (VELA_ERR_TIMEOUT class; no reference counterpart). */
+unsigned vela_device_error(int clear);
+
+/* ---------------------------------------------------------------------------------
+ * W8A16 hi/lo GEMM on the sm_100a tensor cores.
+ * ------------------------------------------------------------------------------ */
+#define VELA_SRC_I8      0     /* planar int8 hi/lo rows + per-row e */
+#define VELA_SRC_X32     1     /* int32 rows quantised on load with e = row_exp(rowmax[row]) */
+#define VELA_SRC_CONV32  2     /* NHWC int32 image, implicit 3x3 pad-1 im2col, K = 9C tap-major, e from vela_conv_e */
+#define VELA_EPI_PLAIN   0     /* y (+ residual), optional per-row max |y| */
+#define VELA_EPI_SPLIT3  1     /* column n -> (Y | Y1 | Y2)[row][n % Cs] */
+#define VELA_EPI_GEGLU   2     /* interleaved a|g columns: Y[row][c] = a * GELU(g) / 2^16, optional row max */
+#define VELA_EPI_GELU    3     /* y * GELU(y) / 2^16 (+ residual), optional row max */
+#define VELA_EPI_QKV     4     /* merged q|k|v: q, k head-quantised (vela_quant_heads layout), v int32 */
+
+/* A operand; struct ASrc of src/gemm_hl.h:13-18 */
+typedef struct vela_asrc {
+    int src;
+    const int8_t* hi; const int8_t* lo; int ld8; const int32_t* e;
+    const int32_t* x; int ldx; const uint32_t* rowmax; int K;
+    const int32_t* img; int H, W, C, stride, Ho, Wo;
+} vela_asrc;
+/* Epilogue; struct AEpi of src/gemm_hl.h:19-25, plus an optional split-K workspace
+ * (used when the output tiles cannot fill the GPU: 2 * splits * Mp * Np * 4 bytes). */
+typedef struct vela_aepi {
+    int epi; int32_t* Y; int ldy; const int32_t* residual;
+    int Cs; int32_t* Y1; int32_t* Y2; const int32_t* Lphi;
+    uint32_t* rowmax;
+    int heads, T, TpQ, TpK, C;
+    int8_t *qhi, *qlo, *khi, *klo; int32_t *qe, *ke; int64_t *qhs, *qls, *qts, *khs, *kls, *kts;
+    void* workspace; size_t workspace_bytes;
+} vela_aepi;
+
+/* Y[r, n] = epi(sat32(rshr((256*Ahi[r].W[n] + Alo[r].W[n] + 128*wsum[n]) * m[n], s[n] - e[r]) + b[n])).
+ * W int8 [Np, ldw] (K-major), cst int32 [Np][4] = {m, s, b, wsum}.  Mp rows of A are addressable,
+ * Mreal rows and Nreal columns are computed.  Replaces k_gemm_hl2 (src/gemm_hl.h:27); all three A
+ * sources and all five epilogues; deep K included (the reference's cuBLASLt path, src/engine.cu:153-157). */
+int vela_gemm_w8a16(void* stream, const vela_asrc* A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                    const int32_t* cst, const vela_aepi* E);
+/* Planar form; replaces k_gemm_hl (src/gemm_hl.h:31-33). */
+int vela_gemm_hl(void* stream, const int8_t* Ahi, const int8_t* Alo, int lda, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                 const int32_t* cst, const int32_t* e, int32_t* Y, int ldy, const int32_t* residual, int epi, int Cs, int32_t* Y1, int32_t* Y2,
+                 const int32_t* Lphi);
+/* e[row] = row_exp(max of pm over the 3x3 window); replaces k_conv_e (src/gemm_hl.h:29). */
+int vela_conv_e(void* stream, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e);
+
 /* ---------------------------------------------------------------------------------
  * Tooling (no reference counterpart): seeded random-init model in the POISDv1
  * format the reference loads (src/poisd.cpp:17-35), with every tensor of the

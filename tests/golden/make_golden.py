@@ -33,8 +33,14 @@ LL = ctypes.c_longlong
 V = ctypes.c_void_p
 
 
+_KEEP = []   # device copies stay referenced until the case ends: a temporary freed inside an argument list
+             # could hand its memory to the next temporary before the kernel reads it
+
+
 def D(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def P(t):
@@ -352,6 +358,8 @@ def main():
             continue
         t0 = time.time()
         c(a.out, rng)
+        torch.cuda.synchronize()
+        _KEEP.clear()
         print(f"{c.__name__}: {time.time() - t0:.1f}s", flush=True)
     if a.model:
         t0 = time.time()

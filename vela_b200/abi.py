@@ -1,0 +1,48 @@
+"""ctypes declarations of the C ABI in include/vela_b200.h (one entry per exported function)."""
+import ctypes
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+U = ctypes.c_uint
+LL = ctypes.c_longlong
+SZ = ctypes.c_size_t
+U64 = ctypes.c_uint64
+
+
+class ASrc(ctypes.Structure):
+    """vela_asrc"""
+    _fields_ = [("src", I), ("hi", P), ("lo", P), ("ld8", I), ("e", P),
+                ("x", P), ("ldx", I), ("rowmax", P), ("K", I),
+                ("img", P), ("H", I), ("W", I), ("C", I), ("stride", I), ("Ho", I), ("Wo", I)]
+
+
+class AEpi(ctypes.Structure):
+    """vela_aepi"""
+    _fields_ = [("epi", I), ("Y", P), ("ldy", I), ("residual", P),
+                ("Cs", I), ("Y1", P), ("Y2", P), ("Lphi", P),
+                ("rowmax", P),
+                ("heads", I), ("T", I), ("TpQ", I), ("TpK", I), ("C", I),
+                ("qhi", P), ("qlo", P), ("khi", P), ("klo", P), ("qe", P), ("ke", P),
+                ("qhs", P), ("qls", P), ("qts", P), ("khs", P), ("kls", P), ("kts", P),
+                ("workspace", P), ("workspace_bytes", SZ)]
+
+
+SRC_I8, SRC_X32, SRC_CONV32 = 0, 1, 2
+EPI_PLAIN, EPI_SPLIT3, EPI_GEGLU, EPI_GELU, EPI_QKV = 0, 1, 2, 3, 4
+
+SIGNATURES = {
+    "vela_last_error": (ctypes.c_char_p, []),
+    "vela_version": (ctypes.c_char_p, []),
+    "vela_device_error": (U, [I]),
+    "vela_synth_model_write": (I, [ctypes.c_char_p, U64]),
+    "vela_gemm_w8a16": (I, [P, ctypes.POINTER(ASrc), I, I, P, I, I, I, I, P, ctypes.POINTER(AEpi)]),
+    "vela_gemm_hl": (I, [P, P, P, I, I, I, P, I, I, I, I, P, P, P, I, P, I, I, P, P, P]),
+    "vela_conv_e": (I, [P, P, I, I, I, I, P]),
+}
+
+
+def declare(L):
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args

@@ -1,0 +1,196 @@
+// Host dispatch of the tcgen05 W8A16 GEMM and its C-ABI entry points.
+// Replaces the reference's k_gemm_hl / k_gemm_hl2 (src/gemm_hl.h:27-33) and,
+// for deep K, its cuBLASLt + k_epilogue path (src/engine.cu:153-157).
+#include "gemm_kernel.cuh"
+#include "host_util.h"
+#include "vela_b200.h"
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+namespace vela {
+
+static __device__ unsigned g_gemm_err;
+
+__global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int splits, int Mp, int Np, int Mreal, int Nreal,
+                                   const int4* __restrict__ cst, const int32_t* __restrict__ e, const uint32_t* __restrict__ rowmax_in, int srcx32,
+                                   int32_t* Y, int ldy, const int32_t* R, int gelu, const int32_t* __restrict__ Lphi, uint32_t* rowmax_out) {
+    const int tpr = Nreal >> 2;
+    const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= size_t(Mreal) * tpr) return;
+    const int r = int(idx / tpr), n = int(idx - size_t(r) * tpr) * 4;
+    int4 hs = make_int4(0, 0, 0, 0), ls = make_int4(0, 0, 0, 0);
+    for (int s = 0; s < splits; ++s) {
+        const int4 h = *reinterpret_cast<const int4*>(partial + (size_t(s) * 2 * Mp + r) * Np + n);
+        const int4 l = *reinterpret_cast<const int4*>(partial + ((size_t(s) * 2 + 1) * Mp + r) * Np + n);
+        hs.x += h.x; hs.y += h.y; hs.z += h.z; hs.w += h.w; ls.x += l.x; ls.y += l.y; ls.z += l.z; ls.w += l.w;
+    }
+    const int er = srcx32 ? row_exp(rowmax_in[r]) : e[r];
+    const int hv[4] = {hs.x, hs.y, hs.z, hs.w}, lv[4] = {ls.x, ls.y, ls.z, ls.w};
+    int y[4]; u32 mx = 0;
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int4 c = cst[n + j];
+        int v = epi_y(hv[j], lv[j], c.x, c.y - er, c.z, 128 * c.w);
+        if (gelu) v = lut_act(v, Lphi);
+        if (R) v = int(sat32(i64(v) + R[size_t(r) * ldy + n + j]));
+        y[j] = v; mx = max(mx, uabs(v));
+    }
+    *reinterpret_cast<int4*>(Y + size_t(r) * ldy + n) = make_int4(y[0], y[1], y[2], y[3]);
+    if (rowmax_out && mx) atomicMax(rowmax_out + r, mx);
+}
+
+// the instantiations live in gemm_inst_*.cu
+#define VELA_GEMM_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm<BN, ST, SRC, EPI>(const GemmArgs&, int, cudaStream_t);
+VELA_GEMM_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_PLAIN)
+VELA_GEMM_EXTERN(64, 6, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_X32, EPI_PLAIN)
+VELA_GEMM_EXTERN(64, 6, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_CONV32, EPI_PLAIN)
+VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_GEGLU) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_GEGLU)
+VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_SPLIT3) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_QKV)
+
+namespace {
+template <int SRC> void dispatch_plain(int BN, const GemmArgs& a, int splits, cudaStream_t st) {
+    if (BN == 64) launch_gemm<64, 6, SRC, EPI_PLAIN>(a, splits, st);
+    else if (BN == 128) launch_gemm<128, 4, SRC, EPI_PLAIN>(a, splits, st);
+    else launch_gemm<256, 4, SRC, EPI_PLAIN>(a, splits, st);
+}
+}  // namespace
+
+// Tile width: the fewest column tiles, then the least padding.
+static int pick_bn(int Nreal, int epi) {
+    if (epi == EPI_QKV || epi == EPI_SPLIT3) return 128;
+    if (epi == EPI_GEGLU) return (Nreal % 256 == 0) ? 256 : 128;
+    if (Nreal % 256 == 0 && Nreal >= 1024) return 256;
+    if (Nreal % 128 == 0) return 128;
+    return 64;
+}
+
+void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                const int32_t* cst, const vela_aepi& E) {
+    VELA_REQUIRE(Mp > 0 && Mreal > 0 && Mreal <= Mp && Nreal > 0 && Nreal <= Np && Kp > 0, "gemm: bad M/N/K");
+    VELA_REQUIRE(Kp % 16 == 0 && ldw % 16 == 0 && ldw >= Kp && Np % 16 == 0, "gemm: Kp, ldw and Np must be multiples of 16");
+    VELA_REQUIRE(W && cst, "gemm: null weights");
+    VELA_REQUIRE((reinterpret_cast<uintptr_t>(W) & 15) == 0, "gemm: W must be 16-byte aligned");
+    GemmArgs a;
+    std::memset(static_cast<void*>(&a), 0, sizeof(a));
+    a.Mreal = Mreal; a.Nreal = Nreal; a.Np = Np; a.Mp = Mp; a.Kp = Kp;
+    a.nkb = ceil_div(Kp, 64);
+    a.cst = reinterpret_cast<const int4*>(cst);
+    a.Y = E.Y; a.ldy = E.ldy; a.R = E.residual; a.Lphi = E.Lphi; a.rowmax_out = E.rowmax;
+    a.gelu = E.epi == VELA_EPI_GELU;
+    a.Cs = E.Cs; a.Y1 = E.Y1; a.Y2 = E.Y2;
+    a.heads = E.heads; a.T = E.T; a.TpQ = E.TpQ; a.TpK = E.TpK; a.Cq = E.C;
+    a.qhi = E.qhi; a.qlo = E.qlo; a.khi = E.khi; a.klo = E.klo; a.qe = E.qe; a.ke = E.ke;
+    a.qhs = E.qhs; a.qls = E.qls; a.qts = E.qts; a.khs = E.khs; a.kls = E.kls; a.kts = E.kts;
+    a.err = device_error_word(&g_gemm_err);
+    const int epi = E.epi == VELA_EPI_GELU ? EPI_PLAIN : E.epi;
+    VELA_REQUIRE(epi >= 0 && epi <= EPI_QKV, "gemm: unknown epilogue");
+    if (epi == EPI_PLAIN) VELA_REQUIRE(E.Y && E.ldy >= Nreal, "gemm: plain epilogue needs Y and ldy >= N");
+    if (epi == EPI_GELU || E.epi == VELA_EPI_GELU || epi == EPI_GEGLU) VELA_REQUIRE(E.Lphi != nullptr, "gemm: GELU/GEGLU need the phi LUT");
+    if (epi == EPI_GEGLU) VELA_REQUIRE(Nreal % 16 == 0 && E.Y && E.ldy >= Nreal / 2 && E.ldy % 4 == 0, "gemm: GEGLU needs N % 16 == 0 and ldy >= N/2, ldy % 4 == 0");
+    if (epi == EPI_SPLIT3) VELA_REQUIRE(E.Cs % 16 == 0 && Nreal == 3 * E.Cs && E.Y && E.Y1 && E.Y2, "gemm: split3 needs N = 3*Cs, Cs % 16 == 0");
+    if (epi == EPI_QKV) VELA_REQUIRE(E.C % 64 == 0 && Nreal == 3 * E.C && E.C == E.heads * 64 && E.T > 0 && Mreal % E.T == 0 && E.Y2 && E.qhi && E.khi,
+                                     "gemm: q|k|v epilogue needs N = 3C, C = 64*heads, rows = B*T");
+
+    const int src = A.src;
+    if (src == VELA_SRC_I8) {
+        VELA_REQUIRE(A.hi && A.lo && A.e && A.ld8 % 16 == 0 && A.ld8 >= Kp, "gemm: int8 planes need hi, lo, e and ld8 % 16 == 0");
+        VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(A.lo) & 15) == 0, "gemm: planes must be 16-byte aligned");
+        a.e = A.e;
+        a.tmA_hi = tmap2d(A.hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, uint64_t(Kp), uint64_t(Mp), uint64_t(A.ld8), 64, 128, Swz::B64);
+        a.tmA_lo = tmap2d(A.lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, uint64_t(Kp), uint64_t(Mp), uint64_t(A.ld8), 64, 128, Swz::B64);
+    } else if (src == VELA_SRC_X32) {
+        VELA_REQUIRE(A.x && A.rowmax && A.K > 0 && A.K % 32 == 0 && A.K <= Kp && A.ldx >= A.K && A.ldx % 4 == 0, "gemm: int32 source needs K % 32 == 0, ldx % 4 == 0");
+        VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.x) & 15) == 0, "gemm: int32 source must be 16-byte aligned");
+        a.x = A.x; a.ldx = A.ldx; a.rowmax_in = A.rowmax; a.K = A.K;
+    } else if (src == VELA_SRC_CONV32) {
+        VELA_REQUIRE(A.img && A.e && A.C % 32 == 0 && A.K == 9 * A.C && A.K <= Kp && A.stride >= 1, "gemm: conv source needs C % 32 == 0, K = 9C");
+        VELA_REQUIRE(A.Ho == (A.H - 1) / A.stride + 1 && A.Wo == (A.W - 1) / A.stride + 1, "gemm: conv output size");
+        VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.img) & 15) == 0, "gemm: image must be 16-byte aligned");
+        a.img = A.img; a.H = A.H; a.W = A.W; a.C = A.C; a.stride = A.stride; a.Ho = A.Ho; a.Wo = A.Wo; a.K = A.K; a.e = A.e;
+    } else {
+        throw Error(VELA_ERR_ARG, "gemm: unknown A source");
+    }
+    if (epi != EPI_PLAIN) VELA_REQUIRE(src == VELA_SRC_I8, "gemm: GEGLU / split3 / q|k|v epilogues take planar int8 operands");
+    const int BN = pick_bn(Nreal, epi);
+    a.tmW = tmap2d(W, CU_TENSOR_MAP_DATA_TYPE_UINT8, uint64_t(Kp), uint64_t(Np), uint64_t(ldw), 64, uint32_t(BN), Swz::B64);
+
+    // split-K when the output tiles cannot fill the GPU and K is deep (exact: integer partial sums)
+    int splits = 1;
+    const int tiles = ceil_div(Np, BN) * ceil_div(Mp, 128), sms = sm_count();
+    if (epi == EPI_PLAIN && E.workspace && tiles * 2 <= sms && a.nkb >= 16) {
+        splits = std::min({sms / tiles, a.nkb / 8, 16});
+        const size_t need = size_t(splits) * 2 * Mp * Np * 4;
+        if (splits < 2 || need > E.workspace_bytes || Nreal % 4 != 0 || E.ldy % 4 != 0) splits = 1;
+    }
+    a.kb_per_split = ceil_div(a.nkb, splits);
+    splits = ceil_div(a.nkb, a.kb_per_split);
+    if (splits > 1) a.partial = static_cast<int32_t*>(E.workspace);
+
+    if (epi == EPI_PLAIN) {
+        if (src == VELA_SRC_I8) dispatch_plain<SRC_I8>(BN, a, splits, st);
+        else if (src == VELA_SRC_X32) dispatch_plain<SRC_X32>(BN, a, splits, st);
+        else dispatch_plain<SRC_CONV32>(BN, a, splits, st);
+    } else if (epi == EPI_GEGLU) {
+        if (BN == 256) launch_gemm<256, 4, SRC_I8, EPI_GEGLU>(a, 1, st); else launch_gemm<128, 4, SRC_I8, EPI_GEGLU>(a, 1, st);
+    } else if (epi == EPI_SPLIT3) {
+        launch_gemm<128, 4, SRC_I8, EPI_SPLIT3>(a, 1, st);
+    } else {
+        launch_gemm<128, 4, SRC_I8, EPI_QKV>(a, 1, st);
+    }
+    if (splits > 1) {
+        const size_t n = size_t(Mreal) * (Nreal / 4);
+        gemm_splitk_reduce<<<unsigned((n + 255) / 256), 256, 0, st>>>(a.partial, splits, Mp, Np, Mreal, Nreal, a.cst, a.e, a.rowmax_in, src == VELA_SRC_X32,
+                                                                     E.Y, E.ldy, E.residual, E.epi == VELA_EPI_GELU, E.Lphi, E.rowmax);
+        VELA_CUDA(cudaGetLastError());
+    }
+}
+
+// conv_e: e[row] = row_exp(max of the pixel maxima over the 3x3 window) (src/gemm_hl.cu:335-341)
+__global__ void conv_e_kernel(const uint32_t* __restrict__ pm, int B, int H, int W, int stride, int Ho, int Wo, int32_t* __restrict__ e) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= B * Ho * Wo) return;
+    const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
+    u32 m = 0;
+    #pragma unroll
+    for (int ky = 0; ky < 3; ++ky)
+        #pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            const int iy = oy * stride - 1 + ky, ix = ox * stride - 1 + kx;
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W) m = max(m, __ldg(pm + (size_t(b) * H + iy) * W + ix));
+        }
+    e[r] = row_exp(m);
+}
+void conv_e(cudaStream_t st, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e) {
+    VELA_REQUIRE(pm && e && B > 0 && H > 0 && W > 0 && stride >= 1, "conv_e: bad arguments");
+    const int Ho = (H - 1) / stride + 1, Wo = (W - 1) / stride + 1, rows = B * Ho * Wo;
+    conv_e_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(pm, B, H, W, stride, Ho, Wo, e);
+}
+}  // namespace vela
+
+using namespace vela;
+
+extern "C" int vela_gemm_w8a16(void* stream, const vela_asrc* A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                               const int32_t* cst, const vela_aepi* E) {
+    return guarded("vela_gemm_w8a16", [&] {
+        VELA_REQUIRE(A && E, "null descriptor");
+        gemm_w8a16(static_cast<cudaStream_t>(stream), *A, Mp, Mreal, W, ldw, Np, Nreal, Kp, cst, *E);
+    });
+}
+extern "C" int vela_gemm_hl(void* stream, const int8_t* Ahi, const int8_t* Alo, int lda, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                            const int32_t* cst, const int32_t* e, int32_t* Y, int ldy, const int32_t* residual, int epi, int Cs, int32_t* Y1, int32_t* Y2,
+                            const int32_t* Lphi) {
+    return guarded("vela_gemm_hl", [&] {
+        vela_asrc A; std::memset(&A, 0, sizeof(A));
+        A.src = VELA_SRC_I8; A.hi = Ahi; A.lo = Alo; A.ld8 = lda; A.e = e;
+        vela_aepi E; std::memset(&E, 0, sizeof(E));
+        E.epi = epi; E.Y = Y; E.ldy = ldy; E.residual = residual; E.Cs = Cs; E.Y1 = Y1; E.Y2 = Y2; E.Lphi = Lphi;
+        gemm_w8a16(static_cast<cudaStream_t>(stream), A, Mp, Mreal, W, ldw, Np, Nreal, Kp, cst, E);
+    });
+}
+extern "C" int vela_conv_e(void* stream, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e) {
+    return guarded("vela_conv_e", [&] { conv_e(static_cast<cudaStream_t>(stream), pm, B, H, W, stride, e); });
+}
+extern "C" unsigned vela_device_error(int clear) {
+    try { return read_device_errors(clear != 0); } catch (...) { return 0xFFFFFFFFu; }
+}

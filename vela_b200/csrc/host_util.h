@@ -1,0 +1,32 @@
+// Host helpers shared by the kernel translation units: TMA tensor maps,
+// per-device error words, small integer utilities.
+#pragma once
+#include "status.h"
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+namespace vela {
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+enum class Swz { None = 0, B32 = 1, B64 = 2, B128 = 3 };
+// Tiled tensor map over a row-major 2-D array: `inner` elements per row (contiguous), `outer` rows,
+// `ld_bytes` between rows; box of boxInner x boxOuter elements.  Out-of-range boxes read zeros.
+CUtensorMap tmap2d(const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer, uint64_t ld_bytes,
+                   uint32_t boxInner, uint32_t boxOuter, Swz swz);
+// 4-D map over an NHWC int32 image [B][H][W][C] with element strides (1, s, s, 1) along (C, W, H, B).
+CUtensorMap tmap_nhwc(const void* base, uint64_t B, uint64_t H, uint64_t W, uint64_t C,
+                      uint32_t boxC, uint32_t boxW, uint32_t boxH, uint32_t boxB, uint32_t stride, Swz swz);
+
+// Address (on the current device) of a translation unit's __device__ error word; cached per device.
+unsigned* device_error_word(const void* symbol);
+// Read and optionally clear every registered error word on the current device (OR of all).
+unsigned read_device_errors(bool clear);
+void register_error_word(const void* symbol);
+
+int current_device();
+int sm_count();
+}  // namespace vela

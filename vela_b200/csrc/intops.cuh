@@ -1,0 +1,88 @@
+// Exact integer primitives of the PoI v2 arithmetic, device (and host) side.
+//
+// Same semantics as the reference's src/intops.cuh:9-66 (the consensus
+// spec of the whole path); restated here from the definitions:
+//   sat32      clamp to int32
+//   rshr(v,s)  round-half-up arithmetic right shift for s >= 0 (shift capped
+//              at 62), saturating left shift for s < 0 (|s| capped at 31,
+//              operand clamped to +-2^(62-|s|)); result saturated to int32
+//   row_exp(m) max(0, bitlen(m) - 15) for 0 <= m < 2^32
+//   quant16    clamp(rshr(v, e), +-32767)
+//   lut16      2049-entry Q16 table on [-16, 16), 10-bit linear interpolation,
+//              0 below the range and 65536 above it
+//   planes     q = 256*hi + lo + 128, hi = q >> 8, lo = (q & 255) - 128
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vela {
+typedef int64_t i64;
+typedef uint32_t u32;
+
+__host__ __device__ __forceinline__ i64 sat32(i64 v) { return v < INT32_MIN ? INT32_MIN : (v > INT32_MAX ? INT32_MAX : v); }
+
+__host__ __device__ __forceinline__ i64 rshr(i64 v, i64 s) {
+    if (s >= 0) {
+        const int p = s > 62 ? 62 : int(s);
+        return sat32((v + ((i64(1) << p) >> 1)) >> p);
+    }
+    const int n = -s > 31 ? 31 : int(-s);
+    const i64 lim = i64(1) << (62 - n);
+    const i64 c = v < -lim ? -lim : (v > lim ? lim : v);
+    return sat32(c * (i64(1) << n));
+}
+// rshr for a shift known to lie in [1, 62]: one add and one shift, then saturate.
+__device__ __forceinline__ i64 rshr_pos(i64 v, int s) { return sat32((v + (i64(1) << (s - 1))) >> s); }
+
+__host__ __device__ __forceinline__ i64 floor_div(i64 a, i64 b) {
+    i64 q = a / b;
+    if ((a % b != 0) && ((a < 0) != (b < 0))) --q;
+    return q;
+}
+
+__device__ __forceinline__ int row_exp(u32 m) { const int e = 17 - __clz(m); return e > 0 ? e : 0; }
+__host__ __forceinline__ int row_exp_host(u32 m) { int e = 0; for (int k = 15; k < 32; ++k) e += (uint64_t(m) >= (uint64_t(1) << k)); return e; }
+
+__device__ __forceinline__ u32 uabs(int v) { return v < 0 ? 0u - u32(v) : u32(v); }
+
+// quant16 of an int32 for e in [0, 17]: floor((v + 2^(e-1)) / 2^e) = (v >> e) + bit (e-1) of v, no overflow.
+__device__ __forceinline__ int quant16(int v, int e) {
+    const int q = e ? (v >> e) + ((v >> (e - 1)) & 1) : v;
+    return min(max(q, -32767), 32767);
+}
+// hi bytes / lo bytes of four 16-bit values packed into one word each
+__device__ __forceinline__ u32 pack_hi4(int q0, int q1, int q2, int q3) {
+    return __byte_perm(__byte_perm(q0, q1, 0x0051), __byte_perm(q2, q3, 0x0051), 0x5410);
+}
+__device__ __forceinline__ u32 pack_lo4(int q0, int q1, int q2, int q3) {
+    return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410) ^ 0x80808080u;
+}
+
+__device__ __forceinline__ int lut16(i64 x, const int32_t* __restrict__ L) {
+    const i64 z = x + (i64(16) << 16);
+    if (z < 0) return 0;
+    if (z >= (i64(32) << 16)) return 65536;
+    const int i = int(z >> 10), f = int(z & 1023);
+    const int a = __ldg(L + i), b = __ldg(L + i + 1);
+    return a + (((b - a) * f) >> 10);
+}
+// x * lut(x) / 2^16, rounded and saturated: SiLU / GELU of a Q16 value
+__device__ __forceinline__ int lut_act(int x, const int32_t* __restrict__ L) { return int(rshr_pos(i64(x) * lut16(x, L), 16)); }
+
+// Exact floor(sqrt(v)) for 0 <= v < 2^62: double seed, then integer correction.
+__host__ __device__ __forceinline__ i64 isqrt(i64 v) {
+    if (v <= 0) return 0;
+    i64 s = i64(sqrt(double(v)));
+    while (s > 0 && s * s > v) --s;
+    while ((s + 1) * (s + 1) <= v) ++s;
+    return s;
+}
+
+// GEMM epilogue y = sat32(rshr(acc * m, s - e) + b) with acc = 256*chi + clo + 128*wsum
+__device__ __forceinline__ int epi_y(int chi, int clo, int m, int sh, int b, int wsum128) {
+    const i64 acc = 256 * i64(chi) + clo + wsum128;
+    const i64 v = acc * i64(m);
+    const i64 r = (sh >= 1 && sh <= 62) ? rshr_pos(v, sh) : rshr(v, sh);
+    return int(sat32(r + b));
+}
+}  // namespace vela

@@ -1,0 +1,606 @@
+// Memory-bound integer kernels of the UNet step and their C-ABI entry points:
+// row quantisation, pixel max, explicit im2col, GroupNorm (stats + apply),
+// LayerNorm, LUT activations, concat / upsample, ChaCha20 noise, finalize,
+// text embedding and the attention operand quantisers.  Semantics follow the
+// reference's src/kernels.cu (cited per kernel); the layouts are B200-first:
+// int4 (16-byte) coalesced loads and stores, warp-per-row reductions held in
+// registers, per-channel accumulation instead of per-element atomics.
+#include "intops.cuh"
+#include "host_util.h"
+#include "vela_b200.h"
+#include <climits>
+#include <cstring>
+
+namespace vela {
+namespace {
+
+__device__ __forceinline__ i64 warp_sum64(i64 v) { for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o); return v; }
+__device__ __forceinline__ int warp_min(int v) { for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o)); return v; }
+__device__ __forceinline__ int warp_max(int v) { for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o)); return v; }
+__device__ __forceinline__ u32 warp_umax(u32 v) { for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o)); return v; }
+
+// floor(a / d) for d >= 1 and |a| < 2^63 with inv = floor((2^64 - 1) / d):
+// q0 = floor(|a| * inv / 2^64) is floor(|a| / d) or one less, one correction step fixes it;
+// a negative numerator uses floor(-x/d) = -floor(x/d) - [x mod d != 0].
+__device__ __forceinline__ i64 floor_div_inv(i64 a, uint64_t d, uint64_t inv) {
+    const uint64_t m = a < 0 ? uint64_t(0) - uint64_t(a) : uint64_t(a);
+    uint64_t q = __umul64hi(m, inv);
+    uint64_t r = m - q * d;
+    if (r >= d) { ++q; r -= d; }
+    if (a >= 0) return i64(q);
+    return r ? -i64(q) - 1 : -i64(q);
+}
+
+// 16 quantised values of one row written as hi / lo bytes at column c (c % 4 == 0)
+__device__ __forceinline__ void store_q4(int8_t* hi, int8_t* lo, int c, int q0, int q1, int q2, int q3) {
+    *reinterpret_cast<u32*>(hi + c) = pack_hi4(q0, q1, q2, q3);
+    *reinterpret_cast<u32*>(lo + c) = pack_lo4(q0, q1, q2, q3);
+}
+// pad columns [C, Kp) of a quantised row with the value 0 = (hi 0, lo -128)
+__device__ __forceinline__ void pad_cols(int8_t* hi, int8_t* lo, int C, int Kp, int lane) {
+    for (int c = C + lane; c < Kp; c += 32) { hi[c] = 0; lo[c] = -128; }
+}
+
+// ---------------------------------------------------------------- row quantisation (src/kernels.cu:42-57,488-497)
+// one warp per row; rows [M, Mpad) become value 0
+__global__ void quant_rows_kernel(const int32_t* __restrict__ X, int M, int Mpad, int K, int ldx, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                                  int32_t* __restrict__ e, int Kp) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= Mpad) return;
+    int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
+    if (r >= M) { for (int k = lane; k < Kp; k += 32) { h[k] = 0; l[k] = -128; } return; }
+    const int32_t* x = X + size_t(r) * ldx;
+    const bool vec = ((K | ldx) & 3) == 0;
+    u32 m = 0;
+    if (vec) { for (int c = lane * 4; c < K; c += 128) { const int4 v = __ldg(reinterpret_cast<const int4*>(x + c)); m = max(m, max(max(uabs(v.x), uabs(v.y)), max(uabs(v.z), uabs(v.w)))); } }
+    else { for (int c = lane; c < K; c += 32) m = max(m, uabs(__ldg(x + c))); }
+    const int ee = row_exp(warp_umax(m));
+    if (lane == 0) e[r] = ee;
+    if (vec) {
+        for (int c = lane * 4; c < K; c += 128) { const int4 v = __ldg(reinterpret_cast<const int4*>(x + c)); store_q4(h, l, c, quant16(v.x, ee), quant16(v.y, ee), quant16(v.z, ee), quant16(v.w, ee)); }
+    } else {
+        for (int c = lane; c < K; c += 32) { const int q = quant16(__ldg(x + c), ee); h[c] = int8_t(q >> 8); l[c] = int8_t((q & 255) - 128); }
+    }
+    pad_cols(h, l, K, Kp, lane);
+}
+
+// ---------------------------------------------------------------- pixel max (src/kernels.cu:106-115)
+__global__ void pixmax_kernel(const int32_t* __restrict__ X, int rows, int C, u32* __restrict__ pm) {
+    const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int32_t* x = X + size_t(r) * C;
+    u32 m = 0;
+    if ((C & 3) == 0) { for (int c = lane * 4; c < C; c += 128) { const int4 v = __ldg(reinterpret_cast<const int4*>(x + c)); m = max(m, max(max(uabs(v.x), uabs(v.y)), max(uabs(v.z), uabs(v.w)))); } }
+    else { for (int c = lane; c < C; c += 32) m = max(m, uabs(__ldg(x + c))); }
+    m = warp_umax(m);
+    if (lane == 0) pm[r] = m;
+}
+
+// ---------------------------------------------------------------- explicit 3x3 im2col (src/kernels.cu:117-170)
+// one warp per output row, K index tap*C + c; rows [rows, Mpad) value 0
+__global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restrict__ pm, int B, int H, int W, int C, int stride, int Ho, int Wo,
+                               int rows, int Mpad, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
+    const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= Mpad) return;
+    int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
+    if (r >= rows) { for (int k = lane; k < Kp; k += 32) { h[k] = 0; l[k] = -128; } return; }
+    const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
+    u32 m = 0;
+    for (int t = 0; t < 9; ++t) {
+        const int iy = oy * stride - 1 + t / 3, ix = ox * stride - 1 + t % 3;
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W) m = max(m, __ldg(pm + (size_t(b) * H + iy) * W + ix));
+    }
+    const int ee = row_exp(m);
+    if (lane == 0) e[r] = ee;
+    const int K = 9 * C;
+    for (int k = lane; k < K; k += 32) {
+        const int tap = k / C, c = k - tap * C, iy = oy * stride - 1 + tap / 3, ix = ox * stride - 1 + tap % 3;
+        const int q = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? quant16(__ldg(X + ((size_t(b) * H + iy) * W + ix) * C + c), ee) : 0;
+        h[k] = int8_t(q >> 8); l[k] = int8_t((q & 255) - 128);
+    }
+    pad_cols(h, l, K, Kp, lane);
+}
+
+// ---------------------------------------------------------------- GroupNorm (src/kernels.cu:173-221,285-305,420-487)
+// Per-(sample, group) accumulation record = vela_gnstat {sum, mn, mx, mean, e, ss, sd}.
+// Pass 1: block = (row chunk, sample); thread = one channel quad for all rows of the chunk (coalesced
+// row-major reads), per-channel sums in registers, then one smem and one global atomic per group.
+__global__ void gn_init_kernel(vela_gnstat* gs, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) { gs[i].sum = 0; gs[i].mn = INT_MAX; gs[i].mx = INT_MIN; gs[i].mean = 0; gs[i].e = 0; gs[i].pad_ = 0; gs[i].ss = 0; gs[i].sd = 0; }
+}
+__global__ void gn_pass1_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
+    __shared__ long long ssum[32]; __shared__ int smn[32], smx[32];
+    const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock), C4 = C >> 2, cg = C >> 5;
+    if (threadIdx.x < 32) { ssum[threadIdx.x] = 0; smn[threadIdx.x] = INT_MAX; smx[threadIdx.x] = INT_MIN; }
+    __syncthreads();
+    for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
+        i64 s[4] = {0, 0, 0, 0}; int mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+        const int32_t* x = X + (size_t(b) * T + t0) * C + c4 * 4;
+        for (int t = t0; t < t1; ++t, x += C) {
+            const int4 v = __ldg(reinterpret_cast<const int4*>(x));
+            s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
+            mn[0] = min(mn[0], v.x); mn[1] = min(mn[1], v.y); mn[2] = min(mn[2], v.z); mn[3] = min(mn[3], v.w);
+            mx[0] = max(mx[0], v.x); mx[1] = max(mx[1], v.y); mx[2] = max(mx[2], v.z); mx[3] = max(mx[3], v.w);
+        }
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int g = (c4 * 4 + k) / cg;
+            atomicAdd(reinterpret_cast<unsigned long long*>(&ssum[g]), (unsigned long long)s[k]);
+            atomicMin(&smn[g], mn[k]); atomicMax(&smx[g], mx[k]);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 32 && t1 > t0) {
+        vela_gnstat* st = gs + b * 32 + threadIdx.x;
+        atomicAdd(reinterpret_cast<unsigned long long*>(&st->sum), (unsigned long long)ssum[threadIdx.x]);
+        atomicMin(&st->mn, smn[threadIdx.x]); atomicMax(&st->mx, smx[threadIdx.x]);
+    }
+}
+// mean and exponent of one group, src/kernels.cu:185-191
+__device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean, int& e) {
+    mean = floor_div(s.sum + n / 2, n);
+    const i64 m = max(i64(s.mx) - mean, mean - i64(s.mn));
+    e = max(0, (m >= (i64(1) << 32) ? 17 : row_exp(u32(m))) - 5);
+}
+__global__ void gn_pass2_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
+    __shared__ long long sss[32]; __shared__ long long smean[32]; __shared__ int se[32];
+    const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock), C4 = C >> 2, cg = C >> 5;
+    if (threadIdx.x < 32) { i64 mean; int e; gn_mean_e(gs[b * 32 + threadIdx.x], i64(T) * cg, mean, e); smean[threadIdx.x] = mean; se[threadIdx.x] = e; sss[threadIdx.x] = 0; }
+    __syncthreads();
+    for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
+        int g[4]; i64 mean[4]; int e[4]; i64 ss[4] = {0, 0, 0, 0};
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) { g[k] = (c4 * 4 + k) / cg; mean[k] = smean[g[k]]; e[k] = se[g[k]]; }
+        const int32_t* x = X + (size_t(b) * T + t0) * C + c4 * 4;
+        for (int t = t0; t < t1; ++t, x += C) {
+            const int4 v = __ldg(reinterpret_cast<const int4*>(x));
+            const int vv[4] = {v.x, v.y, v.z, v.w};
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) { const i64 d = i64(vv[k]) - mean[k]; const i64 dd = e[k] ? ((d >> e[k]) + ((d >> (e[k] - 1)) & 1)) : d; ss[k] += dd * dd; }
+        }
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) atomicAdd(reinterpret_cast<unsigned long long*>(&sss[g[k]]), (unsigned long long)ss[k]);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32 && t1 > t0) atomicAdd(reinterpret_cast<unsigned long long*>(&gs[b * 32 + threadIdx.x].ss), (unsigned long long)sss[threadIdx.x]);
+}
+// mean, e, ss -> var, eps, sd (src/kernels.cu:204-211); also the reciprocal of 2*sd for the apply kernels
+__global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den, uint64_t* inv2sd) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= cnt) return;
+    vela_gnstat s = gs[i];
+    i64 mean; int e; gn_mean_e(s, n, mean, e);
+    s.mean = mean; s.e = e;
+    const i64 var = floor_div(s.ss, n);
+    const int sh = 32 - 2 * e; const i64 one = sh >= 0 ? (i64(1) << sh) : 0;
+    const i64 eps = floor_div(one + den / 2, den);
+    s.sd = isqrt((var + eps) << 16);
+    gs[i] = s;
+    if (inv2sd) inv2sd[i] = s.sd > 0 ? ~0ull / uint64_t(2 * s.sd) : 0;
+}
+// normalise one value: sat32(rshr(floor((d * 2^(24-e) * 2 + sd) / (2 sd)) * g, 16) + beta)
+__device__ __forceinline__ int norm_val(int x, i64 mean, int e, i64 sd, uint64_t inv, int g, int beta) {
+    const i64 d = i64(x) - mean;
+    const i64 yy = floor_div_inv(d * (i64(1) << (25 - e)) + sd, uint64_t(2 * sd), inv);
+    return int(sat32(rshr_pos(yy * g, 16) + beta));
+}
+// Apply: one warp per row.  R4 = int4 chunks per lane held in registers for the quantised output (C <= 128 * R4).
+template <int R4, bool QUANT>
+__global__ void gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs, const uint64_t* __restrict__ inv2sd,
+                                const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
+                                int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
+    const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= M) return;
+    const int b = r / T, cg = C >> 5, C4 = C >> 2;
+    const int32_t* x = X + size_t(r) * C;
+    u32 m = 0;
+    int v[QUANT ? 4 * R4 : 4];
+    #pragma unroll
+    for (int j = 0; j < (QUANT ? R4 : 1 << 20); ++j) {
+        const int c4 = lane + 32 * j;
+        if (c4 >= C4) break;
+        const int c = c4 * 4;
+        const int4 xv = __ldg(reinterpret_cast<const int4*>(x + c)), gv = __ldg(reinterpret_cast<const int4*>(g + c)), bv = __ldg(reinterpret_cast<const int4*>(beta + c));
+        const int xa[4] = {xv.x, xv.y, xv.z, xv.w}, ga[4] = {gv.x, gv.y, gv.z, gv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+        int y[4];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int gi = b * 32 + (c + k) / cg;
+            const vela_gnstat& st = gs[gi];
+            int val = norm_val(xa[k], st.mean, st.e, st.sd, __ldg(inv2sd + gi), ga[k], ba[k]);
+            if (Lsig) val = lut_act(val, Lsig);
+            y[k] = val; m = max(m, uabs(val));
+        }
+        if (QUANT) {
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) v[(4 * j + k) % (QUANT ? 4 * R4 : 4)] = y[k];
+        } else {
+            *reinterpret_cast<int4*>(Y + size_t(r) * C + c) = make_int4(y[0], y[1], y[2], y[3]);
+        }
+    }
+    m = warp_umax(m);
+    if (!QUANT) { if (lane == 0) pm[r] = m; return; }
+    const int ee = row_exp(m);
+    int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
+    if (lane == 0) e[r] = ee;
+    #pragma unroll
+    for (int j = 0; j < R4; ++j) {
+        const int c4 = lane + 32 * j;
+        if (c4 >= C4) break;
+        store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+    }
+    pad_cols(h, l, C, Kp, lane);
+}
+
+// ---------------------------------------------------------------- LayerNorm (src/kernels.cu:223-284,350-419)
+// one warp per row, the row held in registers (C <= 128 * R4, C % 4 == 0)
+template <int R4, bool QUANT, typename GT>
+__global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const GT* __restrict__ g, const GT* __restrict__ beta, i64 den,
+                             int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp, int32_t* __restrict__ Y) {
+    const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= M) return;
+    const int C4 = C >> 2;
+    const int32_t* x = X + size_t(r) * C;
+    int v[4 * R4];
+    i64 sum = 0; int mn = INT_MAX, mx = INT_MIN;
+    #pragma unroll
+    for (int j = 0; j < R4; ++j) {
+        const int c4 = lane + 32 * j;
+        int4 t = make_int4(0, 0, 0, 0);
+        if (c4 < C4) {
+            t = __ldg(reinterpret_cast<const int4*>(x + c4 * 4));
+            sum += i64(t.x) + t.y + t.z + t.w;
+            mn = min(mn, min(min(t.x, t.y), min(t.z, t.w))); mx = max(mx, max(max(t.x, t.y), max(t.z, t.w)));
+        }
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+    }
+    sum = warp_sum64(sum); mn = warp_min(mn); mx = warp_max(mx);
+    const i64 n = C, mean = floor_div(sum + n / 2, n);
+    const i64 rng = max(i64(mx) - mean, mean - i64(mn));
+    const int ex = max(0, (rng >= (i64(1) << 32) ? 17 : row_exp(u32(rng))) - 5);
+    i64 ss = 0;
+    #pragma unroll
+    for (int j = 0; j < R4; ++j) {
+        if (lane + 32 * j >= C4) break;
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) { const i64 d = i64(v[4 * j + k]) - mean; const i64 dd = ex ? ((d >> ex) + ((d >> (ex - 1)) & 1)) : d; ss += dd * dd; }
+    }
+    ss = warp_sum64(ss);
+    const i64 var = floor_div(ss, n);
+    const int shb = 32 - 2 * ex; const i64 one = shb >= 0 ? (i64(1) << shb) : 0;
+    const i64 eps = floor_div(one + den / 2, den);
+    const i64 sd = isqrt((var + eps) << 16);
+    const uint64_t inv = ~0ull / uint64_t(2 * sd);
+    u32 m = 0;
+    #pragma unroll
+    for (int j = 0; j < R4; ++j) {
+        const int c4 = lane + 32 * j;
+        if (c4 >= C4) break;
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int c = c4 * 4 + k;
+            v[4 * j + k] = norm_val(v[4 * j + k], mean, ex, sd, inv, int(g[c]), int(beta[c]));
+            m = max(m, uabs(v[4 * j + k]));
+        }
+        if (!QUANT) *reinterpret_cast<int4*>(Y + size_t(r) * C + c4 * 4) = make_int4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    if (!QUANT) return;
+    const int ee = row_exp(warp_umax(m));
+    int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
+    if (lane == 0) e[r] = ee;
+    #pragma unroll
+    for (int j = 0; j < R4; ++j) {
+        const int c4 = lane + 32 * j;
+        if (c4 >= C4) break;
+        store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+    }
+    pad_cols(h, l, C, Kp, lane);
+}
+
+// ---------------------------------------------------------------- elementwise (src/kernels.cu:537-561)
+__global__ void act_kernel(int32_t* X, size_t n, const int32_t* __restrict__ L) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) X[i] = lut_act(X[i], L);
+}
+__global__ void geglu_kernel(int32_t* A, const int32_t* __restrict__ G, size_t n, const int32_t* __restrict__ L) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+        A[i] = int(rshr_pos(i64(A[i]) * lut_act(G[i], L), 16));
+}
+__global__ void add_kernel(int32_t* X, const int32_t* __restrict__ Y, size_t n) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) X[i] = int(sat32(i64(X[i]) + Y[i]));
+}
+// channel concat, 4 channels per thread (Ca, Cb multiples of 4)
+__global__ void concat_kernel(const int32_t* __restrict__ A, int Ca, const int32_t* __restrict__ Bm, int Cb, size_t rows, int32_t* __restrict__ out) {
+    const int Co4 = (Ca + Cb) >> 2, Ca4 = Ca >> 2;
+    const size_t tot = rows * Co4;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < tot; i += size_t(gridDim.x) * blockDim.x) {
+        const size_t r = i / Co4; const int c4 = int(i - r * Co4);
+        const int4 v = c4 < Ca4 ? __ldg(reinterpret_cast<const int4*>(A + r * Ca) + c4) : __ldg(reinterpret_cast<const int4*>(Bm + r * Cb) + (c4 - Ca4));
+        reinterpret_cast<int4*>(out)[i] = v;
+    }
+}
+// nearest x2 upsample, 4 channels per thread
+__global__ void upsample2_kernel(const int32_t* __restrict__ X, int B, int H, int W, int C, int32_t* __restrict__ out) {
+    const int C4 = C >> 2;
+    const size_t tot = size_t(B) * 4 * H * W * C4;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < tot; i += size_t(gridDim.x) * blockDim.x) {
+        const int c4 = int(i % C4); size_t p = i / C4;
+        const int xo = int(p % (2 * W)); p /= 2 * W; const int yo = int(p % (2 * H)); const int b = int(p / (2 * H));
+        reinterpret_cast<int4*>(out)[i] = __ldg(reinterpret_cast<const int4*>(X + ((size_t(b) * H + (yo >> 1)) * W + (xo >> 1)) * C) + c4);
+    }
+}
+
+// ---------------------------------------------------------------- ChaCha20 noise and finalize (src/kernels.cu:563-599)
+__device__ __forceinline__ u32 rotl(u32 v, int n) { return __funnelshift_l(v, v, n); }
+#define VELA_QR(a, b, c, d) a += b; d ^= a; d = rotl(d, 16); c += d; b ^= c; b = rotl(b, 12); a += b; d ^= a; d = rotl(d, 8); c += d; b ^= c; b = rotl(b, 7);
+// thread = one 64-byte keystream block (RFC 7539 block function, counter = block index, nonce 0) of one sample
+__global__ void noise_kernel(const uint8_t* __restrict__ seeds, int B, const i64* __restrict__ gauss64, const int32_t* __restrict__ gauss32, i64 cin,
+                             int32_t* __restrict__ n, int32_t* __restrict__ x) {
+    const int blk = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (blk >= 512 || b >= B) return;
+    const uint8_t* key = seeds + 32 * b;
+    u32 in[16], st[16];
+    in[0] = 0x61707865u; in[1] = 0x3320646eu; in[2] = 0x79622d32u; in[3] = 0x6b206574u;
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) in[4 + i] = u32(key[4 * i]) | (u32(key[4 * i + 1]) << 8) | (u32(key[4 * i + 2]) << 16) | (u32(key[4 * i + 3]) << 24);
+    in[12] = u32(blk); in[13] = 0; in[14] = 0; in[15] = 0;
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) st[i] = in[i];
+    #pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        VELA_QR(st[0], st[4], st[8], st[12]) VELA_QR(st[1], st[5], st[9], st[13]) VELA_QR(st[2], st[6], st[10], st[14]) VELA_QR(st[3], st[7], st[11], st[15])
+        VELA_QR(st[0], st[5], st[10], st[15]) VELA_QR(st[1], st[6], st[11], st[12]) VELA_QR(st[2], st[7], st[8], st[13]) VELA_QR(st[3], st[4], st[9], st[14])
+    }
+    int32_t* nb = n + size_t(b) * 16384; int32_t* xb = x + size_t(b) * 16384;
+    int nv[32];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const u32 w = st[i] + in[i];
+        nv[2 * i] = gauss32 ? __ldg(gauss32 + (w & 0xffffu)) : int(gauss64[w & 0xffffu]);
+        nv[2 * i + 1] = gauss32 ? __ldg(gauss32 + (w >> 16)) : int(gauss64[w >> 16]);
+    }
+    #pragma unroll
+    for (int i = 0; i < 32; i += 4) *reinterpret_cast<int4*>(nb + blk * 32 + i) = make_int4(nv[i], nv[i + 1], nv[i + 2], nv[i + 3]);
+    // all 32 values of this block share the channel (idx >> 12): channel-major n, NHWC x
+    #pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int idx = blk * 32 + i;
+        xb[(idx & 4095) * 4 + (idx >> 12)] = int(rshr(i64(nv[i]) * cin, 30));
+    }
+}
+__global__ void finalize_kernel(const int32_t* __restrict__ n, const int32_t* __restrict__ eps, int B, i64 sig, uint8_t* __restrict__ out) {
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= size_t(B) * 16384) return;
+    const int b = int(i / 16384), idx = int(i % 16384), c = idx >> 12, p = idx & 4095;
+    const i64 x0 = rshr((i64(n[i]) - eps[size_t(b) * 16384 + p * 4 + c]) * sig, 16);
+    const i64 q = min(max(rshr(x0, 8), i64(-32767)), i64(32767));
+    reinterpret_cast<uint16_t*>(out)[i] = uint16_t(int16_t(q));      // little-endian int16
+}
+__global__ void text_embed_kernel(const int32_t* __restrict__ ids, int T, int rowsPad, const int8_t* __restrict__ tw, const i64* __restrict__ tm,
+                                  const i64* __restrict__ ts, const i64* __restrict__ pos, int D, int32_t* __restrict__ X) {
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= size_t(rowsPad) * D) return;
+    const int t = int(i / D), d = int(i % D);
+    if (t >= T) { X[i] = 0; return; }
+    const int id = ids[t];
+    X[i] = int(sat32(rshr(i64(tw[size_t(id) * D + d]) * tm[id], ts[id] - 16) + pos[size_t(t) * D + d]));
+}
+
+// ---------------------------------------------------------------- attention operands (src/kernels.cu:609-669,799-809)
+// Q/K: one warp per (g, t) row of 64 values (2 per lane); rows t >= T value 0
+__global__ void quant_heads_kernel(const int32_t* __restrict__ X, int B, int T, int C, int heads, int Tp, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                                   int32_t* __restrict__ e, i64* __restrict__ hs, i64* __restrict__ ls, i64* __restrict__ tsum, int tFrom) {
+    const int lane = threadIdx.x & 31;
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int rowsPerG = Tp - tFrom;
+    if (w >= B * heads * rowsPerG) return;
+    const int g = w / rowsPerG, t = tFrom + w % rowsPerG, b = g / heads, h = g % heads;
+    const size_t row = size_t(g) * Tp + t;
+    int8_t* hp = hi + row * 64; int8_t* lp = lo + row * 64;
+    if (t >= T) {
+        *reinterpret_cast<uint16_t*>(hp + 2 * lane) = 0; *reinterpret_cast<uint16_t*>(lp + 2 * lane) = 0x8080;
+        if (lane == 0) { e[row] = 0; hs[row] = 0; ls[row] = -128 * 64; tsum[row] = 0; }
+        return;
+    }
+    const int2 v = __ldg(reinterpret_cast<const int2*>(X + (size_t(b) * T + t) * C + h * 64) + lane);
+    const int ee = row_exp(warp_umax(max(uabs(v.x), uabs(v.y))));
+    const int q0 = quant16(v.x, ee), q1 = quant16(v.y, ee);
+    const int h0 = q0 >> 8, h1 = q1 >> 8, l0 = (q0 & 255) - 128, l1 = (q1 & 255) - 128;
+    *reinterpret_cast<uint16_t*>(hp + 2 * lane) = uint16_t((h0 & 255) | ((h1 & 255) << 8));
+    *reinterpret_cast<uint16_t*>(lp + 2 * lane) = uint16_t((l0 & 255) | ((l1 & 255) << 8));
+    const i64 sh = warp_sum64(h0 + h1), sl = warp_sum64(l0 + l1), st = warp_sum64(q0 + q1);
+    if (lane == 0) { e[row] = ee; hs[row] = sh; ls[row] = sl; tsum[row] = st; }
+}
+// V column statistics: block = (g, t-chunk of 256 rows) x 64 dims; column max (atomic)
+__global__ void quant_v_max_kernel(const int32_t* __restrict__ X, int Tk, int C, int heads, u32* __restrict__ colmax) {
+    __shared__ u32 sm[4][64];
+    const int g = blockIdx.y, b = g / heads, h = g % heads, d = threadIdx.x & 63, ts = threadIdx.x >> 6;
+    const int t0 = blockIdx.x * 256, t1 = min(Tk, t0 + 256);
+    const int32_t* x = X + size_t(b) * Tk * C + h * 64 + d;
+    u32 m = 0;
+    for (int t = t0 + ts; t < t1; t += 4) m = max(m, uabs(__ldg(x + size_t(t) * C)));
+    sm[ts][d] = m;
+    __syncthreads();
+    if (ts == 0) { m = max(max(sm[0][d], sm[1][d]), max(sm[2][d], sm[3][d])); if (m) atomicMax(colmax + g * 64 + d, m); }
+}
+// transposed quantised write [G][64][Tkp] + per-column sums of the true values: block = (g, 64-row t tile)
+__global__ void quant_v_write_kernel(const int32_t* __restrict__ X, int Tk, int C, int heads, int Tkp, const u32* __restrict__ colmax,
+                                     int8_t* __restrict__ vh, int8_t* __restrict__ vl, int32_t* __restrict__ ev, i64* __restrict__ vsum) {
+    __shared__ int tile[64][65];
+    const int g = blockIdx.y, t0 = blockIdx.x * 64, b = g / heads, h = g % heads;
+    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+    for (int r = ty; r < 64; r += 4) { const int t = t0 + r; tile[r][tx] = t < Tk ? __ldg(X + (size_t(b) * Tk + t) * C + h * 64 + tx) : 0; }
+    __syncthreads();
+    for (int d = ty; d < 64; d += 4) {
+        const int e = row_exp(colmax[g * 64 + d]);
+        const int t = t0 + tx;
+        const int q = t < Tk ? quant16(tile[tx][d], e) : 0;
+        const size_t o = (size_t(g) * 64 + d) * Tkp + t;
+        vh[o] = int8_t(q >> 8); vl[o] = int8_t((q & 255) - 128);
+        i64 s = q;
+        for (int o2 = 16; o2; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+        if ((tx & 31) == 0 && s) atomicAdd(reinterpret_cast<unsigned long long*>(vsum + g * 64 + d), (unsigned long long)s);
+        if (blockIdx.x == 0 && tx == 0) ev[g * 64 + d] = e;
+    }
+}
+
+inline unsigned grid1(size_t n, int per = 256) { return unsigned(std::min<size_t>((n + per - 1) / per, size_t(148) * 32)); }
+}  // namespace
+
+// ================================================================ host launchers (used by the engine and the C ABI)
+void quant_rows(cudaStream_t st, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    VELA_REQUIRE(X && hi && lo && e && M > 0 && K > 0 && Kp >= K && ldx >= K, "quant_rows: bad arguments");
+    const int Mpad = (M + 31) / 32 * 32;
+    quant_rows_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, M, Mpad, K, ldx, hi, lo, e, Kp);
+}
+void pixmax(cudaStream_t st, const int32_t* X, int rows, int C, uint32_t* pm) {
+    VELA_REQUIRE(X && pm && rows > 0 && C > 0, "pixmax: bad arguments");
+    pixmax_kernel<<<ceil_div(rows, 8), 256, 0, st>>>(X, rows, C, pm);
+}
+void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H, int W, int C, int stride, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    VELA_REQUIRE(X && pm && hi && lo && e && Kp >= 9 * C && stride >= 1, "im2col3: bad arguments");
+    const int Ho = (H - 1) / stride + 1, Wo = (W - 1) / stride + 1, rows = B * Ho * Wo, Mpad = (rows + 31) / 32 * 32;
+    im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+}
+static int gn_rows_per_block(int B, int T) { int chunks = std::max(1, (148 * 4) / std::max(1, B)); return std::max(1, ceil_div(T, chunks)); }
+// statistics only (accumulate + finish); inv2sd optional
+void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs, uint64_t* inv2sd) {
+    VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 128 == 0 && C <= 4 * 1024, "gn_stats: C must be a multiple of 128 (32 groups of a multiple of 4)");
+    const int cnt = B * 32, rpb = gn_rows_per_block(B, T);
+    gn_init_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt);
+    const dim3 grid(ceil_div(T, rpb), B);
+    const int threads = std::min(1024, (C / 4 + 31) / 32 * 32);
+    gn_pass1_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
+    gn_pass2_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
+    gn_finish_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt, i64(T) * (C / 32), den, inv2sd);
+}
+void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const uint64_t* inv2sd, const int32_t* g, const int32_t* beta,
+              const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    VELA_REQUIRE(X && gs && inv2sd && g && beta && C % 128 == 0, "gn_apply: bad arguments");
+    const int M = B * T; const unsigned blocks = ceil_div(M, 8);
+    if (hi) {
+        VELA_REQUIRE(lo && e && Kp >= C && C <= 1280, "gn_apply: quantised output needs C <= 1280");
+        if (C <= 384) gn_apply_kernel<3, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        else if (C <= 640) gn_apply_kernel<5, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        else gn_apply_kernel<10, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+    } else {
+        VELA_REQUIRE(Y && pm, "gn_apply: int32 output needs Y and pm");
+        gn_apply_kernel<1, false><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+    }
+}
+template <bool QUANT, typename GT>
+static void lnorm_dispatch(cudaStream_t st, const int32_t* X, int M, int C, const GT* g, const GT* beta, i64 den, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int32_t* Y) {
+    const unsigned blocks = ceil_div(M, 8);
+    if (C <= 384) lnorm_kernel<3, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
+    else if (C <= 640) lnorm_kernel<5, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
+    else if (C <= 1280) lnorm_kernel<10, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
+    else throw Error(VELA_ERR_ARG, "lnorm: C must be <= 1280");
+}
+void lnorm_q(cudaStream_t st, const int32_t* X, int M, int C, const int32_t* g, const int32_t* beta, i64 den, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    VELA_REQUIRE(X && g && beta && hi && lo && e && C % 4 == 0 && Kp >= C, "lnorm_q: bad arguments");
+    lnorm_dispatch<true, int32_t>(st, X, M, C, g, beta, den, hi, lo, e, Kp, nullptr);
+}
+void lnorm(cudaStream_t st, const int32_t* X, int M, int C, const i64* g, const i64* beta, i64 den, int32_t* Y) {
+    VELA_REQUIRE(X && g && beta && Y && C % 4 == 0, "lnorm: bad arguments");
+    lnorm_dispatch<false, i64>(st, X, M, C, g, beta, den, nullptr, nullptr, nullptr, 0, Y);
+}
+void act(cudaStream_t st, int32_t* X, size_t n, const int32_t* L) { act_kernel<<<grid1(n), 256, 0, st>>>(X, n, L); }
+void geglu(cudaStream_t st, int32_t* A, const int32_t* G, size_t n, const int32_t* L) { geglu_kernel<<<grid1(n), 256, 0, st>>>(A, G, n, L); }
+void add(cudaStream_t st, int32_t* X, const int32_t* Y, size_t n) { add_kernel<<<grid1(n), 256, 0, st>>>(X, Y, n); }
+void concat(cudaStream_t st, const int32_t* A, int Ca, const int32_t* Bm, int Cb, int rows, int32_t* out) {
+    VELA_REQUIRE(A && Bm && out && Ca % 4 == 0 && Cb % 4 == 0, "concat: channel counts must be multiples of 4");
+    concat_kernel<<<grid1(size_t(rows) * (Ca + Cb) / 4), 256, 0, st>>>(A, Ca, Bm, Cb, size_t(rows), out);
+}
+void upsample2(cudaStream_t st, const int32_t* X, int B, int H, int W, int C, int32_t* out) {
+    VELA_REQUIRE(X && out && C % 4 == 0, "upsample2: C must be a multiple of 4");
+    upsample2_kernel<<<grid1(size_t(B) * 4 * H * W * C / 4), 256, 0, st>>>(X, B, H, W, C, out);
+}
+void noise(cudaStream_t st, const uint8_t* seeds, int B, const i64* gauss64, const int32_t* gauss32, i64 cin, int32_t* n, int32_t* x) {
+    VELA_REQUIRE(seeds && (gauss64 || gauss32) && n && x && B > 0, "noise: bad arguments");
+    noise_kernel<<<dim3(4, B), 128, 0, st>>>(seeds, B, gauss64, gauss32, cin, n, x);
+}
+void finalize(cudaStream_t st, const int32_t* n, const int32_t* eps, int B, i64 sig, uint8_t* out) {
+    VELA_REQUIRE(n && eps && out && B > 0, "finalize: bad arguments");
+    finalize_kernel<<<ceil_div(B * 16384, 256), 256, 0, st>>>(n, eps, B, sig, out);
+}
+void text_embed(cudaStream_t st, const int32_t* ids, int T, int rowsPad, const int8_t* tw, const i64* tm, const i64* ts, const i64* pos, int D, int32_t* X) {
+    VELA_REQUIRE(ids && tw && tm && ts && pos && X, "text_embed: bad arguments");
+    text_embed_kernel<<<ceil_div(rowsPad * D, 256), 256, 0, st>>>(ids, T, rowsPad, tw, tm, ts, pos, D, X);
+}
+void quant_heads(cudaStream_t st, const int32_t* X, int B, int T, int C, int heads, int Tp, int8_t* hi, int8_t* lo, int32_t* e, i64* hs, i64* ls, i64* tsum, int tFrom) {
+    VELA_REQUIRE(hi && lo && e && hs && ls && tsum && C == heads * 64 && Tp >= T, "quant_heads: bad arguments");
+    if (tFrom < T) VELA_REQUIRE(X != nullptr, "quant_heads: null X");
+    const int rows = B * heads * (Tp - tFrom);
+    if (rows > 0) quant_heads_kernel<<<ceil_div(rows, 8), 256, 0, st>>>(X, B, T, C, heads, Tp, hi, lo, e, hs, ls, tsum, tFrom);
+}
+void quant_v(cudaStream_t st, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vh, int8_t* vl, int32_t* ev, i64* vsum, uint32_t* colmax) {
+    VELA_REQUIRE(X && vh && vl && ev && vsum && colmax && C == heads * 64 && Tkp >= Tk && Tkp % 64 == 0, "quant_v: bad arguments");
+    const int G = B * heads;
+    VELA_CUDA(cudaMemsetAsync(colmax, 0, size_t(G) * 64 * 4, st));
+    VELA_CUDA(cudaMemsetAsync(vsum, 0, size_t(G) * 64 * 8, st));
+    quant_v_max_kernel<<<dim3(ceil_div(Tk, 256), G), 256, 0, st>>>(X, Tk, C, heads, colmax);
+    quant_v_write_kernel<<<dim3(Tkp / 64, G), 256, 0, st>>>(X, Tk, C, heads, Tkp, colmax, vh, vl, ev, vsum);
+}
+}  // namespace vela
+
+// ================================================================ C ABI (src/kernels.h)
+using namespace vela;
+#define ST static_cast<cudaStream_t>(stream)
+
+extern "C" int vela_quant_rows(void* stream, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    return guarded("vela_quant_rows", [&] { quant_rows(ST, X, M, K, ldx, hi, lo, e, Kp); });
+}
+extern "C" int vela_pixmax(void* stream, const int32_t* X, int rows, int C, uint32_t* pm) {
+    return guarded("vela_pixmax", [&] { pixmax(ST, X, rows, C, pm); });
+}
+extern "C" int vela_im2col3(void* stream, const int32_t* X, const uint32_t* pm, int B, int H, int W, int C, int stride, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    return guarded("vela_im2col3", [&] { im2col3(ST, X, pm, B, H, W, C, stride, hi, lo, e, Kp); });
+}
+extern "C" int vela_gn_stats(void* stream, const int32_t* X, int B, int T, int C, int groups, long long den, vela_gnstat* gs) {
+    return guarded("vela_gn_stats", [&] { VELA_REQUIRE(groups == 32, "gn_stats: 32 groups"); gn_stats(ST, X, B, T, C, den, gs, nullptr); });
+}
+extern "C" int vela_gn_apply_row(void* stream, const int32_t* X, int B, int T, int C, int groups, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
+                                 const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp, uint64_t* inv_scratch) {
+    return guarded("vela_gn_apply_row", [&] {
+        VELA_REQUIRE(groups == 32 && inv_scratch, "gn_apply_row: 32 groups and a B*32 x 8-byte scratch for the divisor reciprocals");
+        // reciprocals of 2*sd from the finished statistics (gn_finish recomputes the same record)
+        vela_gnstat* gsm = const_cast<vela_gnstat*>(gs);
+        (void)gsm;
+        gn_apply_prepare(ST, gs, B * 32, inv_scratch);
+        gn_apply(ST, X, B, T, C, gs, inv_scratch, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+    });
+}
+extern "C" int vela_lnorm_q(void* stream, const int32_t* X, int M, int C, const int32_t* g, const int32_t* beta, long long den, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
+    return guarded("vela_lnorm_q", [&] { lnorm_q(ST, X, M, C, g, beta, den, hi, lo, e, Kp); });
+}
+extern "C" int vela_lnorm(void* stream, const int32_t* X, int M, int C, const int64_t* g, const int64_t* beta, long long den, int32_t* Y) {
+    return guarded("vela_lnorm", [&] { lnorm(ST, X, M, C, g, beta, den, Y); });
+}
+extern "C" int vela_act(void* stream, int32_t* X, size_t n, const int32_t* L) { return guarded("vela_act", [&] { act(ST, X, n, L); }); }
+extern "C" int vela_geglu(void* stream, int32_t* A, const int32_t* G, size_t n, const int32_t* L) { return guarded("vela_geglu", [&] { geglu(ST, A, G, n, L); }); }
+extern "C" int vela_add(void* stream, int32_t* X, const int32_t* Y, size_t n) { return guarded("vela_add", [&] { add(ST, X, Y, n); }); }
+extern "C" int vela_concat(void* stream, const int32_t* A, int Ca, const int32_t* Bm, int Cb, int rows, int32_t* out) {
+    return guarded("vela_concat", [&] { concat(ST, A, Ca, Bm, Cb, rows, out); });
+}
+extern "C" int vela_upsample2(void* stream, const int32_t* X, int B, int H, int W, int C, int32_t* out) {
+    return guarded("vela_upsample2", [&] { upsample2(ST, X, B, H, W, C, out); });
+}
+extern "C" int vela_noise(void* stream, const uint8_t* seeds, int B, const int64_t* gauss, long long cin, int32_t* n, int32_t* x) {
+    return guarded("vela_noise", [&] { noise(ST, seeds, B, gauss, nullptr, cin, n, x); });
+}
+extern "C" int vela_finalize(void* stream, const int32_t* n, const int32_t* eps, int B, long long sig, uint8_t* out) {
+    return guarded("vela_finalize", [&] { finalize(ST, n, eps, B, sig, out); });
+}
+extern "C" int vela_text_embed(void* stream, const int32_t* ids, int T, int rowsPad, const int8_t* tw, const int64_t* tm, const int64_t* ts, const int64_t* pos, int D, int32_t* X) {
+    return guarded("vela_text_embed", [&] { text_embed(ST, ids, T, rowsPad, tw, tm, ts, pos, D, X); });
+}
+extern "C" int vela_quant_heads(void* stream, const int32_t* X, int B, int T, int C, int heads, int Tp, int8_t* hi, int8_t* lo, int32_t* e, int64_t* hs, int64_t* ls, int64_t* tsum) {
+    return guarded("vela_quant_heads", [&] { quant_heads(ST, X, B, T, C, heads, Tp, hi, lo, e, hs, ls, tsum, 0); });
+}
+extern "C" int vela_quant_heads_pad(void* stream, int G, int T, int Tp, int8_t* hi, int8_t* lo, int32_t* e, int64_t* hs, int64_t* ls, int64_t* tsum) {
+    return guarded("vela_quant_heads_pad", [&] { quant_heads(ST, nullptr, 1, T, G * 64, G, Tp, hi, lo, e, hs, ls, tsum, T); });
+}
+extern "C" int vela_quant_v(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum, uint32_t* scratch) {
+    return guarded("vela_quant_v", [&] { quant_v(ST, X, B, Tk, C, heads, Tkp, vt_hi, vt_lo, ev, vsum, scratch); });
+}
