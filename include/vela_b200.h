@@ -90,6 +90,49 @@ int vela_gemm_hl(void* stream, const int8_t* Ahi, const int8_t* Alo, int lda, in
 int vela_conv_e(void* stream, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e);
 
 /* ---------------------------------------------------------------------------------
+ * Row / memory-bound operators (src/kernels.h).  int64 arguments (den, cin, sig) and
+ * int64 LUTs / parameters keep the reference's types.
+ * ------------------------------------------------------------------------------ */
+/* Per-row power-of-two quantisation of X[M, K] (row stride ldx) into hi/lo [*, Kp] + e[M]; columns
+ * [K, Kp) and rows [M, align32(M)) are written as the value 0.  k_quant_rows (src/kernels.h:14). */
+int vela_quant_rows(void* stream, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+/* pm[r] = max_c |X[r, c]|.  k_pixmax (src/kernels.h:19). */
+int vela_pixmax(void* stream, const int32_t* X, int rows, int C, uint32_t* pm);
+/* 3x3 pad-1 im2col with per-output-pixel quantisation, K index tap*C + c.  k_im2col3 (src/kernels.h:21-22). */
+int vela_im2col3(void* stream, const int32_t* X, const uint32_t* pm, int B, int H, int W, int C, int stride, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+/* GroupNorm statistics of X[B, T, C] (32 groups): the complete GnStat records.  k_gn_stats1 + k_gn_stats2 (src/kernels.h:24-29). */
+int vela_gn_stats(void* stream, const int32_t* X, int B, int T, int C, int groups, long long den, vela_gnstat* gs);
+/* GroupNorm apply (+ optional SiLU LUT): int32 Y + pixel max pm, or (hi != NULL) planes + e.  k_gn_apply_row (src/kernels.h:61-62). */
+int vela_gn_apply_row(void* stream, const int32_t* X, int B, int T, int C, int groups, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
+                      const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+/* LayerNorm rows of X[M, C] -> quantised planes + e.  k_lnorm_q (src/kernels.h:59). */
+int vela_lnorm_q(void* stream, const int32_t* X, int M, int C, const int32_t* g, const int32_t* beta, long long den, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+/* LayerNorm rows of X[M, C] -> int32.  k_lnorm (src/kernels.h:31). */
+int vela_lnorm(void* stream, const int32_t* X, int M, int C, const int64_t* g, const int64_t* beta, long long den, int32_t* Y);
+/* x = sat32(rshr(x * lut(x), 16)) in place.  k_act (src/kernels.h:32). */
+int vela_act(void* stream, int32_t* X, size_t n, const int32_t* L);
+/* a = sat32(rshr(a * gelu(g), 16)).  k_geglu (src/kernels.h:33). */
+int vela_geglu(void* stream, int32_t* A, const int32_t* G, size_t n, const int32_t* L);
+/* x = sat32(x + y).  k_add (src/kernels.h:34). */
+int vela_add(void* stream, int32_t* X, const int32_t* Y, size_t n);
+/* out[r] = [A[r] | B[r]] (Ca, Cb multiples of 4).  k_concat (src/kernels.h:35). */
+int vela_concat(void* stream, const int32_t* A, int Ca, const int32_t* Bm, int Cb, int rows, int32_t* out);
+/* nearest x2 upsample of NHWC X.  k_upsample2 (src/kernels.h:36). */
+int vela_upsample2(void* stream, const int32_t* X, int B, int H, int W, int C, int32_t* out);
+/* ChaCha20(seed) keystream -> u16 -> gauss LUT -> n [B,4,4096] channel-major, x = rshr(n*cin, 30) NHWC.  k_noise (src/kernels.h:38). */
+int vela_noise(void* stream, const uint8_t* seeds, int B, const int64_t* gauss, long long cin, int32_t* n, int32_t* x);
+/* x0 = rshr((n - eps)*sig, 16); out = clamp(rshr(x0, 8)) int16 LE [B, 32768 bytes].  k_finalize (src/kernels.h:40). */
+int vela_finalize(void* stream, const int32_t* n, const int32_t* eps, int B, long long sig, uint8_t* out);
+/* token embedding + position.  k_text_embed (src/kernels.h:42). */
+int vela_text_embed(void* stream, const int32_t* ids, int T, int rowsPad, const int8_t* tw, const int64_t* tm, const int64_t* ts, const int64_t* pos, int D, int32_t* X);
+/* Q/K head quantisation [G, Tp, 64] + e, hs, ls, tsum; rows t >= T value 0.  k_quant_heads (src/kernels.h:45-46). */
+int vela_quant_heads(void* stream, const int32_t* X, int B, int T, int C, int heads, int Tp, int8_t* hi, int8_t* lo, int32_t* e, int64_t* hs, int64_t* ls, int64_t* tsum);
+/* rows [T, Tp) of G head-quantised operands set to the value 0.  k_quant_heads_pad (src/kernels.h:57). */
+int vela_quant_heads_pad(void* stream, int G, int T, int Tp, int8_t* hi, int8_t* lo, int32_t* e, int64_t* hs, int64_t* ls, int64_t* tsum);
+/* V column quantisation, transposed [G, 64, Tkp] + ev, vsum; scratch u32[G*64].  k_quant_v (src/kernels.h:49-50). */
+int vela_quant_v(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum, uint32_t* scratch);
+
+/* ---------------------------------------------------------------------------------
  * Tooling (no reference counterpart): seeded random-init model in the POISDv1
  * format the reference loads (src/poisd.cpp:17-35), with every tensor of the
  * SD-2.1 UNet and 23-layer text encoder.  Host path.  ~1.19 GB.

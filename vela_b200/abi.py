@@ -38,6 +38,24 @@ SIGNATURES = {
     "vela_gemm_w8a16": (I, [P, ctypes.POINTER(ASrc), I, I, P, I, I, I, I, P, ctypes.POINTER(AEpi)]),
     "vela_gemm_hl": (I, [P, P, P, I, I, I, P, I, I, I, I, P, P, P, I, P, I, I, P, P, P]),
     "vela_conv_e": (I, [P, P, I, I, I, I, P]),
+    "vela_quant_rows": (I, [P, P, I, I, I, P, P, P, I]),
+    "vela_pixmax": (I, [P, P, I, I, P]),
+    "vela_im2col3": (I, [P, P, P, I, I, I, I, I, P, P, P, I]),
+    "vela_gn_stats": (I, [P, P, I, I, I, I, LL, P]),
+    "vela_gn_apply_row": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P, P, P, I]),
+    "vela_lnorm_q": (I, [P, P, I, I, P, P, LL, P, P, P, I]),
+    "vela_lnorm": (I, [P, P, I, I, P, P, LL, P]),
+    "vela_act": (I, [P, P, SZ, P]),
+    "vela_geglu": (I, [P, P, P, SZ, P]),
+    "vela_add": (I, [P, P, P, SZ]),
+    "vela_concat": (I, [P, P, I, P, I, I, P]),
+    "vela_upsample2": (I, [P, P, I, I, I, I, P]),
+    "vela_noise": (I, [P, P, I, P, LL, P, P]),
+    "vela_finalize": (I, [P, P, P, I, LL, P]),
+    "vela_text_embed": (I, [P, P, I, I, P, P, P, P, I, P]),
+    "vela_quant_heads": (I, [P, P, I, I, I, I, I, P, P, P, P, P, P]),
+    "vela_quant_heads_pad": (I, [P, I, I, I, P, P, P, P, P, P]),
+    "vela_quant_v": (I, [P, P, I, I, I, I, I, P, P, P, P, P]),
 }
 
 

@@ -8,6 +8,7 @@
 #include "intops.cuh"
 #include "host_util.h"
 #include "vela_b200.h"
+#include <algorithm>
 #include <climits>
 #include <cstring>
 
@@ -166,8 +167,8 @@ __global__ void gn_pass2_kernel(const int32_t* __restrict__ X, int T, int C, int
     __syncthreads();
     if (threadIdx.x < 32 && t1 > t0) atomicAdd(reinterpret_cast<unsigned long long*>(&gs[b * 32 + threadIdx.x].ss), (unsigned long long)sss[threadIdx.x]);
 }
-// mean, e, ss -> var, eps, sd (src/kernels.cu:204-211); also the reciprocal of 2*sd for the apply kernels
-__global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den, uint64_t* inv2sd) {
+// mean, e, ss -> var, eps, sd (src/kernels.cu:204-211)
+__global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= cnt) return;
     vela_gnstat s = gs[i];
@@ -178,7 +179,6 @@ __global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den, uint6
     const i64 eps = floor_div(one + den / 2, den);
     s.sd = isqrt((var + eps) << 16);
     gs[i] = s;
-    if (inv2sd) inv2sd[i] = s.sd > 0 ? ~0ull / uint64_t(2 * s.sd) : 0;
 }
 // normalise one value: sat32(rshr(floor((d * 2^(24-e) * 2 + sd) / (2 sd)) * g, 16) + beta)
 __device__ __forceinline__ int norm_val(int x, i64 mean, int e, i64 sd, uint64_t inv, int g, int beta) {
@@ -186,52 +186,68 @@ __device__ __forceinline__ int norm_val(int x, i64 mean, int e, i64 sd, uint64_t
     const i64 yy = floor_div_inv(d * (i64(1) << (25 - e)) + sd, uint64_t(2 * sd), inv);
     return int(sat32(rshr_pos(yy * g, 16) + beta));
 }
-// Apply: one warp per row.  R4 = int4 chunks per lane held in registers for the quantised output (C <= 128 * R4).
+// Apply: one warp per row, 8 rows per block.  Mean, e, sd and the reciprocal of 2*sd of the 32 groups
+// are staged in shared memory: once per block when T % 8 == 0 (a block then never straddles two
+// samples), else once per warp.
+// R4 = int4 chunks per lane held in registers for the quantised output (C <= 128 * R4).
 template <int R4, bool QUANT>
-__global__ void gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs, const uint64_t* __restrict__ inv2sd,
+__global__ void gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs,
                                 const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
                                 int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
-    const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    __shared__ long long sm_mean[8][32], sm_sd[8][32]; __shared__ unsigned long long sm_inv[8][32]; __shared__ int sm_e[8][32];
+    const int lane = threadIdx.x & 31, r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const bool perBlock = (T & 7) == 0;
+    const int slot = perBlock ? 0 : (threadIdx.x >> 5);
+    if (perBlock ? threadIdx.x < 32 : r < M) {
+        const int bb = perBlock ? (blockIdx.x * 8) / T : r / T;
+        const vela_gnstat st = gs[bb * 32 + lane];
+        sm_mean[slot][lane] = st.mean; sm_e[slot][lane] = st.e; sm_sd[slot][lane] = st.sd;
+        sm_inv[slot][lane] = st.sd > 0 ? ~0ull / uint64_t(2 * st.sd) : 0ull;
+    }
+    __syncthreads();
     if (r >= M) return;
-    const int b = r / T, cg = C >> 5, C4 = C >> 2;
+    const long long* s_mean = sm_mean[slot]; const long long* s_sd = sm_sd[slot]; const unsigned long long* s_inv = sm_inv[slot]; const int* s_e = sm_e[slot];
+    const int cg = C >> 5, C4 = C >> 2;
     const int32_t* x = X + size_t(r) * C;
     u32 m = 0;
     int v[QUANT ? 4 * R4 : 4];
     #pragma unroll
-    for (int j = 0; j < (QUANT ? R4 : 1 << 20); ++j) {
+    for (int j = 0; j < (QUANT ? R4 : 64); ++j) {
         const int c4 = lane + 32 * j;
         if (c4 >= C4) break;
         const int c = c4 * 4;
         const int4 xv = __ldg(reinterpret_cast<const int4*>(x + c)), gv = __ldg(reinterpret_cast<const int4*>(g + c)), bv = __ldg(reinterpret_cast<const int4*>(beta + c));
         const int xa[4] = {xv.x, xv.y, xv.z, xv.w}, ga[4] = {gv.x, gv.y, gv.z, gv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+        const int g0 = c / cg, cut = (g0 + 1) * cg;      // groups of >= 4 channels: at most one boundary in a quad
         int y[4];
         #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int gi = b * 32 + (c + k) / cg;
-            const vela_gnstat& st = gs[gi];
-            int val = norm_val(xa[k], st.mean, st.e, st.sd, __ldg(inv2sd + gi), ga[k], ba[k]);
+            const int gi = cg >= 4 ? ((c + k) >= cut ? g0 + 1 : g0) : (c + k) / cg;
+            int val = norm_val(xa[k], s_mean[gi], s_e[gi], s_sd[gi], s_inv[gi], ga[k], ba[k]);
             if (Lsig) val = lut_act(val, Lsig);
             y[k] = val; m = max(m, uabs(val));
         }
-        if (QUANT) {
+        if constexpr (QUANT) {
             #pragma unroll
-            for (int k = 0; k < 4; ++k) v[(4 * j + k) % (QUANT ? 4 * R4 : 4)] = y[k];
+            for (int k = 0; k < 4; ++k) v[4 * j + k] = y[k];
         } else {
             *reinterpret_cast<int4*>(Y + size_t(r) * C + c) = make_int4(y[0], y[1], y[2], y[3]);
         }
     }
     m = warp_umax(m);
-    if (!QUANT) { if (lane == 0) pm[r] = m; return; }
-    const int ee = row_exp(m);
-    int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
-    if (lane == 0) e[r] = ee;
-    #pragma unroll
-    for (int j = 0; j < R4; ++j) {
-        const int c4 = lane + 32 * j;
-        if (c4 >= C4) break;
-        store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+    if constexpr (!QUANT) { if (lane == 0) pm[r] = m; return; }
+    else {
+        const int ee = row_exp(m);
+        int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
+        if (lane == 0) e[r] = ee;
+        #pragma unroll
+        for (int j = 0; j < R4; ++j) {
+            const int c4 = lane + 32 * j;
+            if (c4 >= C4) break;
+            store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+        }
+        pad_cols(h, l, C, Kp, lane);
     }
-    pad_cols(h, l, C, Kp, lane);
 }
 
 // ---------------------------------------------------------------- LayerNorm (src/kernels.cu:223-284,350-419)
@@ -464,29 +480,29 @@ void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H
     im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
 }
 static int gn_rows_per_block(int B, int T) { int chunks = std::max(1, (148 * 4) / std::max(1, B)); return std::max(1, ceil_div(T, chunks)); }
-// statistics only (accumulate + finish); inv2sd optional
-void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs, uint64_t* inv2sd) {
-    VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 128 == 0 && C <= 4 * 1024, "gn_stats: C must be a multiple of 128 (32 groups of a multiple of 4)");
+// statistics: accumulate sum/min/max, then the squared deviations, then mean/e/sd per (sample, group)
+void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs) {
+    VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 32 == 0 && C % 4 == 0 && C <= 4096, "gn_stats: C must be a multiple of 32 (32 groups)");
     const int cnt = B * 32, rpb = gn_rows_per_block(B, T);
     gn_init_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt);
     const dim3 grid(ceil_div(T, rpb), B);
     const int threads = std::min(1024, (C / 4 + 31) / 32 * 32);
     gn_pass1_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
     gn_pass2_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
-    gn_finish_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt, i64(T) * (C / 32), den, inv2sd);
+    gn_finish_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt, i64(T) * (C / 32), den);
 }
-void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const uint64_t* inv2sd, const int32_t* g, const int32_t* beta,
+void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
               const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
-    VELA_REQUIRE(X && gs && inv2sd && g && beta && C % 128 == 0, "gn_apply: bad arguments");
+    VELA_REQUIRE(X && gs && g && beta && C % 32 == 0, "gn_apply: C must be a multiple of 32 (32 groups)");
     const int M = B * T; const unsigned blocks = ceil_div(M, 8);
     if (hi) {
         VELA_REQUIRE(lo && e && Kp >= C && C <= 1280, "gn_apply: quantised output needs C <= 1280");
-        if (C <= 384) gn_apply_kernel<3, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
-        else if (C <= 640) gn_apply_kernel<5, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
-        else gn_apply_kernel<10, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        if (C <= 384) gn_apply_kernel<3, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        else if (C <= 640) gn_apply_kernel<5, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        else gn_apply_kernel<10, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
     } else {
         VELA_REQUIRE(Y && pm, "gn_apply: int32 output needs Y and pm");
-        gn_apply_kernel<1, false><<<blocks, 256, 0, st>>>(X, M, T, C, gs, inv2sd, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        gn_apply_kernel<1, false><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
     }
 }
 template <bool QUANT, typename GT>
@@ -558,17 +574,13 @@ extern "C" int vela_im2col3(void* stream, const int32_t* X, const uint32_t* pm, 
     return guarded("vela_im2col3", [&] { im2col3(ST, X, pm, B, H, W, C, stride, hi, lo, e, Kp); });
 }
 extern "C" int vela_gn_stats(void* stream, const int32_t* X, int B, int T, int C, int groups, long long den, vela_gnstat* gs) {
-    return guarded("vela_gn_stats", [&] { VELA_REQUIRE(groups == 32, "gn_stats: 32 groups"); gn_stats(ST, X, B, T, C, den, gs, nullptr); });
+    return guarded("vela_gn_stats", [&] { VELA_REQUIRE(groups == 32, "gn_stats: 32 groups"); gn_stats(ST, X, B, T, C, den, gs); });
 }
 extern "C" int vela_gn_apply_row(void* stream, const int32_t* X, int B, int T, int C, int groups, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
-                                 const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp, uint64_t* inv_scratch) {
+                                 const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
     return guarded("vela_gn_apply_row", [&] {
-        VELA_REQUIRE(groups == 32 && inv_scratch, "gn_apply_row: 32 groups and a B*32 x 8-byte scratch for the divisor reciprocals");
-        // reciprocals of 2*sd from the finished statistics (gn_finish recomputes the same record)
-        vela_gnstat* gsm = const_cast<vela_gnstat*>(gs);
-        (void)gsm;
-        gn_apply_prepare(ST, gs, B * 32, inv_scratch);
-        gn_apply(ST, X, B, T, C, gs, inv_scratch, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        VELA_REQUIRE(groups == 32, "gn_apply_row: 32 groups");
+        gn_apply(ST, X, B, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
     });
 }
 extern "C" int vela_lnorm_q(void* stream, const int32_t* X, int M, int C, const int32_t* g, const int32_t* beta, long long den, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
