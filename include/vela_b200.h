@@ -133,6 +133,21 @@ int vela_quant_heads_pad(void* stream, int G, int T, int Tp, int8_t* hi, int8_t*
 int vela_quant_v(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum, uint32_t* scratch);
 
 /* ---------------------------------------------------------------------------------
+ * Exact integer attention on the tensor cores.
+ * ------------------------------------------------------------------------------ */
+/* out[b, q, h*64 + d] for q < Tq (+ row max |out| into rowmax, optional) from head-quantised Q
+ * [G, Tqp, 64] (+ eq, qhs, qls), K [G, Tkp, 64] (+ ek, ksum = true-value row sums) and V^T
+ * [G, 64, Tkp] (+ ev, vsum); G = B * heads; Tqp, Tkp multiples of 64, Tk <= Tkp <= 4096.
+ * lexp32 is the exp LUT (>= 1025 int32 entries).  Replaces k_fused_attention (src/kernels.h:72-78);
+ * gmx / gr (the reference's between-pass scratch) are accepted and unused: one CTA runs all three
+ * exact passes of a query tile, so the row maxima and reciprocals stay in registers. */
+int vela_fused_attention(void* stream, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, const int64_t* qhs, const int64_t* qls,
+                         const int8_t* khi, const int8_t* klo, const int32_t* ek, const int64_t* ksum,
+                         const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const int64_t* vsum,
+                         int B, int heads, int Tq, int Tqp, int Tk, int Tkp, int causal, const int32_t* lexp32, int C,
+                         int32_t* gmx, int64_t* gr, int32_t* out, uint32_t* rowmax);
+
+/* ---------------------------------------------------------------------------------
  * Tooling (no reference counterpart): seeded random-init model in the POISDv1
  * format the reference loads (src/poisd.cpp:17-35), with every tensor of the
  * SD-2.1 UNet and 23-layer text encoder.  Host path.  ~1.19 GB.

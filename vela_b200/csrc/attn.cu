@@ -27,6 +27,7 @@
 #include "host_util.h"
 #include "vela_b200.h"
 #include <climits>
+#include <cstring>
 
 namespace vela {
 namespace {
@@ -212,11 +213,14 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         int mx = INT_MIN; uint64_t sum = 0; uint32_t rlo = 0, rhi = 0; int psum = 0;
         int uses[2] = {0, 0};
         bool ok = true;
-        for (int it = 0; it < nIt && ok; ++it) {
+        // Every warp runs all nIt iterations and every named barrier, also after a timed-out wait
+        // (then it skips the work), so no warp can be left waiting on a barrier the others skipped.
+        for (int it = 0; it < nIt; ++it) {
             const int pass = it / nT, j = it % nT, ks = it % KS;
             const int b = pass < 2 ? (it & 1) : 0;
-            if (!mbar_wait(&qk_full[b], uses[b] & 1, a.err, DEVERR_TIMEOUT_FULL)) { ok = false; break; }
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], uses[b] & 1, a.err, DEVERR_TIMEOUT_FULL));
             ++uses[b];
+            if (ok) {
             tc_fence_after();
             const int32_t* ekp = reinterpret_cast<const int32_t*>(sm + OFF_KAUX + ks * KAUX_BYTES) + half * 32;
             const i64* ksp = reinterpret_cast<const i64*>(sm + OFF_KAUX + ks * KAUX_BYTES + 256) + half * 32;
@@ -236,11 +240,13 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
                 const int shmin = shq - ekmax, shmax = shq - ekmin;
                 const int cls = __all_sync(0xffffffffu, shmin >= 16) ? 0 : (__all_sync(0xffffffffu, shmin >= 5 && shmax <= 15) ? 1 : 2);
                 int s[16];
+                uint32_t vmask = 0;          // validity by key position (a valid score may itself saturate to INT_MIN)
                 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
                     const int T = (xx[u] << 8) + ll[u] + cq + kc[u];
                     const int key = kbase + c * 16 + u;
                     const bool valid = full || (key < a.Tk && !(a.causal && key > q));
+                    vmask |= uint32_t(valid) << u;
                     s[u] = valid ? score_c(hh[u], T, shq - ekk[u], cls) : INT_MIN;
                 }
                 if (pass == 0) {
@@ -249,8 +255,8 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
                 } else {
                     #pragma unroll
                     for (int u = 0; u < 16; u += 2) {
-                        const uint32_t e0 = s[u] == INT_MIN ? 0u : lut_exp(uint32_t(mx) - uint32_t(s[u]), lut2);
-                        const uint32_t e1 = s[u + 1] == INT_MIN ? 0u : lut_exp(uint32_t(mx) - uint32_t(s[u + 1]), lut2);
+                        const uint32_t e0 = (vmask >> u) & 1u ? lut_exp(uint32_t(mx) - uint32_t(s[u]), lut2) : 0u;
+                        const uint32_t e1 = (vmask >> (u + 1)) & 1u ? lut_exp(uint32_t(mx) - uint32_t(s[u + 1]), lut2) : 0u;
                         if (pass == 1) sum += uint64_t(e0 + e1);            // each E <= 2^30: a pair fits 32 bits
                         else {
                             const uint32_t ev2[2] = {e0, e1};
@@ -278,7 +284,8 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             __syncwarp();
             if (lane == 0) { mbar_arrive(&qk_free[b]); mbar_arrive(&k_empty[ks]); }
             if (pass == 2) {
-                if (!mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
+                if (ok) {
                 uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
                 *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
                 *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_h[4], pw_h[5], pw_h[6], pw_h[7]);
@@ -287,6 +294,8 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(p_full);
+                }
+            }
             }
             if (j == nT - 1 && pass < 2) {         // combine the two key halves of each row
                 red[half * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
@@ -305,7 +314,7 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         red[half * 128 + rl] = psum;
         asm volatile("bar.sync 1, 256;" ::: "memory");
         const i64 ps = i64(psum) + red[(half ^ 1) * 128 + rl];
-        const bool done = ok && mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC);
+        const bool done = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC));
         tc_fence_after();
         if (done) {
             const int bidx = g / a.heads, h = g % a.heads;

@@ -89,8 +89,8 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
     if (epi == EPI_GELU || E.epi == VELA_EPI_GELU || epi == EPI_GEGLU) VELA_REQUIRE(E.Lphi != nullptr, "gemm: GELU/GEGLU need the phi LUT");
     if (epi == EPI_GEGLU) VELA_REQUIRE(Nreal % 16 == 0 && E.Y && E.ldy >= Nreal / 2 && E.ldy % 4 == 0, "gemm: GEGLU needs N % 16 == 0 and ldy >= N/2, ldy % 4 == 0");
     if (epi == EPI_SPLIT3) VELA_REQUIRE(E.Cs % 16 == 0 && Nreal == 3 * E.Cs && E.Y && E.Y1 && E.Y2, "gemm: split3 needs N = 3*Cs, Cs % 16 == 0");
-    if (epi == EPI_QKV) VELA_REQUIRE(E.C % 64 == 0 && Nreal == 3 * E.C && E.C == E.heads * 64 && E.T > 0 && Mreal % E.T == 0 && E.Y2 && E.qhi && E.khi,
-                                     "gemm: q|k|v epilogue needs N = 3C, C = 64*heads, rows = B*T");
+    if (epi == EPI_QKV) VELA_REQUIRE(E.C % 64 == 0 && (Nreal == 3 * E.C || Nreal == E.C) && E.C == E.heads * 64 && E.T > 0 && Mreal % E.T == 0 && E.qhi &&
+                                     (Nreal == E.C || (E.Y2 && E.khi)), "gemm: q|k|v epilogue needs N = 3C (or N = C: q only), C = 64*heads, rows = B*T");
 
     const int src = A.src;
     if (src == VELA_SRC_I8) {

@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(320, 1) gemm_w8a16_kernel(const __grid_constan
         }
         // ------------------------------------------------------------ epilogue
         asm volatile("bar.sync 1, 256;" ::: "memory");          // column constants staged (epilogue warps only)
-        const bool ok = mbar_wait(accb, 0, a.err, DEVERR_TIMEOUT_ACC);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(accb, 0, a.err, DEVERR_TIMEOUT_ACC));   // warp-uniform: tcgen05.ld is warp-collective
         tc_fence_after();
         if (ok) {
             const int q = warp & 3, h = (warp - 2) >> 2;
