@@ -148,6 +148,45 @@ int vela_fused_attention(void* stream, const int8_t* qhi, const int8_t* qlo, con
                          int32_t* gmx, int64_t* gr, int32_t* out, uint32_t* rowmax);
 
 /* ---------------------------------------------------------------------------------
+ * Engine: one denoising step of the SD-turbo UNet per batch (src/engine.h:16-124).
+ * A model holds the prepared weights of one GPU and is shared read-only by its engines; an engine
+ * (one per host thread, the reference's "lane") owns a stream, an activation arena and two
+ * pipeline slots, each with its own CUDA graph of the whole step and pinned I/O buffers.
+ * ------------------------------------------------------------------------------ */
+typedef struct vela_model vela_model;
+typedef struct vela_engine vela_engine;
+typedef struct vela_engine_config {
+    int batch;              /* inferences per step (EngineConfig::batch) */
+    int graph;              /* 1: replay one CUDA graph per slot (EngineConfig::graph); 0: eager launches */
+    size_t arena_bytes;     /* activation arena; 0 = 1 GiB + 512 MiB per inference */
+} vela_engine_config;
+typedef void (*vela_tap_fn)(void* user, const char* name, const int32_t* data, size_t count);
+
+/* Load a POISD model file onto `device` (DevModel::load, src/engine.cu:11-70). NULL on failure. */
+vela_model* vela_model_load(int device, const char* path);
+void vela_model_free(vela_model* m);
+size_t vela_model_bytes(const vela_model* m);
+/* Engine(dm, cfg) (src/engine.cu:114-129). NULL on failure. */
+vela_engine* vela_engine_create(const vela_model* m, const vela_engine_config* cfg);
+void vela_engine_destroy(vela_engine* e);
+/* Text encoder + cross-attention K/V of a prompt of BPE token ids (Engine::setPrompt, src/engine.cu:528-574). */
+int vela_engine_set_prompt(vela_engine* e, const int32_t* tokens, int n);
+/* host: the 77 x 1024 int32 context of the current prompt (the text encoder's output). */
+int vela_engine_context(vela_engine* e, int32_t* ctx);
+/* host seeds [batch][32] -> host x0 [batch][32768] (int16 LE), synchronous (Engine::run, src/engine.cu:650-677). */
+int vela_engine_run(vela_engine* e, const uint8_t* seeds, uint8_t* x0);
+/* two batches in flight: submit enqueues (Engine::submit), collect waits for the oldest (Engine::collect). */
+int vela_engine_submit(vela_engine* e, const uint8_t* seeds);
+int vela_engine_collect(vela_engine* e, uint8_t* x0);
+/* one eager step handing every block output (host int32) to `tap` in UNet order (no reference counterpart: parity taps). */
+int vela_engine_step_taps(vela_engine* e, const uint8_t* seeds, uint8_t* x0, vela_tap_fn tap, void* user);
+int vela_engine_in_flight(const vela_engine* e);
+int vela_engine_batch(const vela_engine* e);
+size_t vela_engine_arena_peak(const vela_engine* e);
+void* vela_engine_stream(const vela_engine* e);
+double vela_engine_last_ms(const vela_engine* e);   /* device time of the last vela_engine_run, ms */
+
+/* ---------------------------------------------------------------------------------
  * Tooling (no reference counterpart): seeded random-init model in the POISDv1
  * format the reference loads (src/poisd.cpp:17-35), with every tensor of the
  * SD-2.1 UNet and 23-layer text encoder.  Host path.  ~1.19 GB.

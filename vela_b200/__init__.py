@@ -44,3 +44,101 @@ def synth_model_write(path, seed=1):
     """Write the seeded random-init POISD model (SD-2.1 UNet + text encoder shapes) to `path`."""
     check(lib().vela_synth_model_write(path.encode(), int(seed)))
     return path
+
+
+class Model:
+    """Weights of one GPU (vela_model_load): a POISD file prepared for the tcgen05 kernels."""
+
+    def __init__(self, path, device=0):
+        self.h = lib().vela_model_load(int(device), path.encode())
+        if not self.h:
+            raise VelaError(-5, lib().vela_last_error().decode())
+        self.device = device
+
+    @property
+    def bytes(self):
+        return lib().vela_model_bytes(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vela_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Engine:
+    """One lane: stream + arena + two graph slots (vela_engine_*).  Host numpy buffers in and out."""
+
+    def __init__(self, model, batch=8, graph=True, arena_bytes=0):
+        from .abi import EngineConfig
+        import numpy as np
+        self._np = np
+        cfg = EngineConfig(int(batch), int(bool(graph)), int(arena_bytes))
+        self.model = model
+        self.h = lib().vela_engine_create(model.h, ctypes.byref(cfg))
+        if not self.h:
+            raise VelaError(-1, lib().vela_last_error().decode())
+        self.batch = batch
+
+    def set_prompt(self, tokens):
+        t = self._np.ascontiguousarray(tokens, self._np.int32)
+        check(lib().vela_engine_set_prompt(self.h, t.ctypes.data_as(ctypes.c_void_p), len(t)))
+
+    def context(self):
+        out = self._np.zeros((77, 1024), self._np.int32)
+        check(lib().vela_engine_context(self.h, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def _seeds(self, seeds):
+        s = self._np.ascontiguousarray(seeds, self._np.uint8)
+        assert s.size == 32 * self.batch, "seeds must be [batch, 32] bytes"
+        return s
+
+    def run(self, seeds):
+        s = self._seeds(seeds)
+        x0 = self._np.zeros((self.batch, 32768), self._np.uint8)
+        check(lib().vela_engine_run(self.h, s.ctypes.data_as(ctypes.c_void_p), x0.ctypes.data_as(ctypes.c_void_p)))
+        return x0
+
+    def submit(self, seeds):
+        s = self._seeds(seeds)
+        check(lib().vela_engine_submit(self.h, s.ctypes.data_as(ctypes.c_void_p)))
+
+    def collect(self, out=None):
+        x0 = out if out is not None else self._np.zeros((self.batch, 32768), self._np.uint8)
+        check(lib().vela_engine_collect(self.h, x0.ctypes.data_as(ctypes.c_void_p)))
+        return x0
+
+    def step_taps(self, seeds, tap):
+        """one eager step; tap(name, int32 numpy array) for every block output"""
+        s = self._seeds(seeds)
+        x0 = self._np.zeros((self.batch, 32768), self._np.uint8)
+        TAP = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_size_t)
+        cb = TAP(lambda u, name, data, n: tap(name.decode(), self._np.ctypeslib.as_array(data, shape=(n,))))
+        check(lib().vela_engine_step_taps(self.h, s.ctypes.data_as(ctypes.c_void_p), x0.ctypes.data_as(ctypes.c_void_p),
+                                          ctypes.cast(cb, ctypes.c_void_p), None))
+        return x0
+
+    @property
+    def last_ms(self):
+        return lib().vela_engine_last_ms(self.h)
+
+    @property
+    def arena_peak(self):
+        return lib().vela_engine_arena_peak(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vela_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

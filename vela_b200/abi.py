@@ -57,7 +57,28 @@ SIGNATURES = {
     "vela_quant_heads_pad": (I, [P, I, I, I, P, P, P, P, P, P]),
     "vela_quant_v": (I, [P, P, I, I, I, I, I, P, P, P, P, P]),
     "vela_fused_attention": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, P, P]),
+    "vela_model_load": (P, [I, ctypes.c_char_p]),
+    "vela_model_free": (None, [P]),
+    "vela_model_bytes": (SZ, [P]),
+    "vela_engine_create": (P, [P, P]),
+    "vela_engine_destroy": (None, [P]),
+    "vela_engine_set_prompt": (I, [P, P, I]),
+    "vela_engine_context": (I, [P, P]),
+    "vela_engine_run": (I, [P, P, P]),
+    "vela_engine_submit": (I, [P, P]),
+    "vela_engine_collect": (I, [P, P]),
+    "vela_engine_step_taps": (I, [P, P, P, P, P]),
+    "vela_engine_in_flight": (I, [P]),
+    "vela_engine_batch": (I, [P]),
+    "vela_engine_arena_peak": (SZ, [P]),
+    "vela_engine_stream": (P, [P]),
+    "vela_engine_last_ms": (ctypes.c_double, [P]),
 }
+
+
+class EngineConfig(ctypes.Structure):
+    """vela_engine_config"""
+    _fields_ = [("batch", I), ("graph", I), ("arena_bytes", SZ)]
 
 
 def declare(L):
