@@ -1,0 +1,452 @@
+#!/usr/bin/env python3
+"""Throughput of the exact-integer SD-turbo UNet step on B200s: UNet inferences/s, batch 8 x 2 lanes per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vela|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N ...
+
+A step is one UNet denoising step (noise -> UNet -> x0) on every lane of every GPU: 2 lanes x batch 8 =
+16 inferences per GPU.  Inferences are independent; each GPU (one process each) runs its own model copy on
+a disjoint block of seeds with no collective on the data path ("scaling": "weak").
+
+Our arm (--impl vela), one JSON line from rank 0:
+  value       device-timed: the step graphs replayed on device-resident seeds (vela_engine_launch_device),
+              both lanes' streams bracketed by CUDA events; K steps; max over ranks.
+  e2e         the public API a user calls (Engine.submit / Engine.collect from one host thread per lane,
+              the reference's runBench pattern, src/main.cpp:111-162): host seeds in, host x0 out, the H2D and
+              D2H copies inside the timed region; wall clock between synchronised barriers, max over ranks.
+  roofline    the dominant kernel of the step (exact attention at the largest self-attention shape,
+              8 x 5 heads x 4096 tokens x 64), timed live with CUDA events on the stream it is launched on.
+  cpu_baseline the CPU restatement of the integer spec (oracle/, OpenMP over the host cores), one bounded
+              sample: one step at batch 1 (rank 0, N = 1 only).
+  x0 check    the golden seeds of the reference engine's fixture must give the reference engine's x0 bytes,
+              and every rank must produce the same x0 for the same seeds.
+
+The reference arm (--impl reference) runs the reference engine itself, compiled from the reference's own
+sources (oracle/_ref/libvela_ref.so, built by `make -C oracle ref`), through its own Engine::submit /
+collect with one host thread per lane, on the same model file, batch, lanes and steps.
+"""
+import argparse
+import hashlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = [320, 736, 3240]
+MODEL_SEED = 1
+METRIC = "UNet inferences/s (SD-turbo step, batch 8 x 2 lanes per GPU, bit-exact x0)"
+UNIT = "inferences/s"
+# algorithmic int8 work of one self-attention launch at 8 x 5 heads x 4096 x 4096 x 64: QK^T and PV,
+# each a 16-bit x 16-bit product carried as 4 int8 planes -> 2 * 4 * 8*5*4096*4096*64 MACs, 2 ops per MAC
+ATTN_SHAPE = dict(B=8, heads=5, T=4096)
+ATTN_OPS = 2 * 4 * 2 * 8 * 5 * 4096 * 4096 * 64
+ATTN_PROFILE = os.path.join(ROOT, "profiles", "attention_self_b8h5t4096.md")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["vela", "reference"], default="vela")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--lanes", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["attention"], default=None,
+                    help="run only the named kernel at its bench shape (for profiler captures) and exit")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    return a
+
+
+# ------------------------------------------------------------------ process group / devices
+class Ranks:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self):
+        import torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v):
+        from vela_b200.dist import max_over_ranks
+        import torch
+        return max_over_ranks(v, torch.device("cuda", self.local)) if self.pg else float(v)
+
+    def agree(self, digest):
+        from vela_b200.dist import digests_agree
+        import torch
+        return digests_agree(digest, torch.device("cuda", self.local)) if self.pg else True
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi samples every 200 ms while running (the GPU's clocks and throttle reasons)"""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu, self.p, self.f = gpu, None, None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.TemporaryFile("w+")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.seek(0)
+        rows = [[c.strip() for c in line.split(",")] for line in self.f if line.count(",") >= 7]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, reasons, smax, power = [], set(), None, []
+        for r in rows:
+            try:
+                sm.append(float(r[1])); smax = float(r[2]); power.append(float(r[3]))
+            except ValueError:
+                continue
+            for i, n in enumerate(names):
+                if r[4 + i].lower() == "active":
+                    reasons.add(n)
+        load = [s for s, p in zip(sm, power) if p > 300] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def model_file(rank):
+    import vela_b200 as V
+    path = os.path.join(tempfile.gettempdir(), f"vela_synth_seed{MODEL_SEED}_rank{rank}.poisd")
+    if not os.path.exists(path) or os.path.getsize(path) < (1 << 30):
+        V.synth_model_write(path, MODEL_SEED)
+    return path
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the roofline kernel, from the committed ncu summary (None if not captured yet)"""
+    try:
+        with open(ATTN_PROFILE) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1].split()[0])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ the dominant kernel, live
+class AttentionCase:
+    """Quantised operands of one self-attention at 8 x 5 heads x 4096 x 64 (activations uniform over the int16
+    range, seeded), built by the library's own quantisers; launch() runs vela_fused_attention once."""
+
+    def __init__(self, device):
+        import torch
+        import vela_b200 as V
+        self.t, self.V, self.L = torch, V, V.lib()
+        B, heads, T = ATTN_SHAPE["B"], ATTN_SHAPE["heads"], ATTN_SHAPE["T"]
+        C, G, Tp = 64 * heads, B * heads, (T + 127) // 128 * 128
+        g = torch.Generator(device=device); g.manual_seed(2)
+        d = lambda *s, dt: torch.zeros(s, dtype=dt, device=device)
+        X = [torch.randint(-32768, 32768, (B, T, C), generator=g, device=device, dtype=torch.int32) for _ in range(3)]
+        self.q = [d(G, Tp, 64, dt=torch.int8), d(G, Tp, 64, dt=torch.int8), d(G, Tp, dt=torch.int32)] + [d(G, Tp, dt=torch.int64) for _ in range(3)]
+        self.k = [d(G, Tp, 64, dt=torch.int8), d(G, Tp, 64, dt=torch.int8), d(G, Tp, dt=torch.int32)] + [d(G, Tp, dt=torch.int64) for _ in range(3)]
+        self.v = [d(G, 64, Tp, dt=torch.int8), d(G, 64, Tp, dt=torch.int8), d(G, 64, dt=torch.int32), d(G, 64, dt=torch.int64)]
+        colmax = d(G, 64, dt=torch.int32)
+        self.lexp = torch.from_numpy(np.rint(1073741824.0 * np.exp(-np.arange(1025) / 64.0)).astype(np.int32)).to(device)
+        self.out = d(B, T, C, dt=torch.int32); self.rm = d(B * T, dt=torch.int32)
+        self.stream = torch.cuda.current_stream(device)
+        P = lambda x: x.data_ptr()
+        st = self.stream.cuda_stream
+        V.check(self.L.vela_quant_heads(st, P(X[0]), B, T, C, heads, Tp, *[P(x) for x in self.q]))
+        V.check(self.L.vela_quant_heads(st, P(X[1]), B, T, C, heads, Tp, *[P(x) for x in self.k]))
+        V.check(self.L.vela_quant_v(st, P(X[2]), B, T, C, heads, Tp, *[P(x) for x in self.v], P(colmax)))
+        self.args = (P(self.q[0]), P(self.q[1]), P(self.q[2]), P(self.q[3]), P(self.q[4]), P(self.k[0]), P(self.k[1]), P(self.k[2]),
+                     P(self.k[5]), P(self.v[0]), P(self.v[1]), P(self.v[2]), P(self.v[3]), B, heads, T, Tp, T, Tp, 0,
+                     P(self.lexp), C, None, None, P(self.out), P(self.rm))
+        del X
+        torch.cuda.synchronize(device)
+
+    def launch(self):
+        self.V.check(self.L.vela_fused_attention(self.stream.cuda_stream, *self.args))
+
+    def time_ms(self, warmup=3, iters=10):
+        torch = self.t
+        for _ in range(warmup):
+            self.launch()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(self.stream)
+        for _ in range(iters):
+            self.launch()
+        e1.record(self.stream)
+        e1.synchronize()
+        assert self.L.vela_device_error(1) == 0, "attention kernel reported a device error"
+        return e0.elapsed_time(e1) / iters
+
+
+# ------------------------------------------------------------------ CPU baseline (the oracle, bounded sample)
+def cpu_baseline(path):
+    from oracle import pyoracle as O
+    from vela_b200.dist import golden_seeds
+    cores = os.cpu_count() or 1
+    O.lib().or_set_threads(cores)
+    m = O.Model(path)
+    m.set_prompt(PROMPT)
+    t0 = time.perf_counter()
+    m.step(golden_seeds(1))
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": 1.0 / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"one UNet step at batch 1 (1 of the 16 inferences of a GPU step) on the oracle's C restatement, "
+                      f"OpenMP x {cores} threads: {dt:.2f} s"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_vela(a, R):
+    import torch
+    import vela_b200 as V
+    from vela_b200.dist import seed_block, golden_seeds
+    dev = torch.device("cuda", R.local)
+    path = model_file(R.rank)
+    model = V.Model(path, R.local)
+    lanes = [V.Engine(model, batch=a.batch, graph=True) for _ in range(a.lanes)]
+    for e in lanes:
+        e.set_prompt(PROMPT)
+
+    # parity of the bench's own engine: golden seeds -> the reference engine's x0 (tests/golden/engine.npz)
+    gs = golden_seeds(a.batch)
+    x0 = lanes[0].run(gs)
+    gold = np.load(os.path.join(ROOT, "tests", "golden", "engine.npz"))
+    ref_ok = bool(np.array_equal(x0[: len(gold["x0"])], gold["x0"]))
+    same = R.agree(hashlib.sha256(x0.tobytes()).digest())
+
+    # device-resident inputs: seeds of every (rank, lane, step) already in HBM
+    n_steps = a.warmup + a.steps
+    seeds = torch.from_numpy(np.stack([np.stack([seed_block(R.rank, l, s, a.batch) for s in range(n_steps)]) for l in range(a.lanes)])).to(dev)
+    out = torch.empty((a.lanes, a.batch, 32768), dtype=torch.uint8, device=dev)
+    streams = [torch.cuda.ExternalStream(e.stream, device=dev) for e in lanes]
+    main = torch.cuda.current_stream(dev)
+
+    def launch(step):
+        for l, e in enumerate(lanes):
+            e.launch_device(seeds[l, step].data_ptr(), out[l].data_ptr())
+
+    for s in range(a.warmup):
+        launch(s)
+    torch.cuda.synchronize(dev)
+    kernels_per_step = sum(e.graph_kernels for e in lanes)
+    R.barrier(); torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ends = [torch.cuda.Event() for _ in lanes]
+    with Clocks(R.local) as clk:
+        e0.record(main)
+        for st in streams:
+            st.wait_event(e0)
+        for s in range(a.steps):
+            launch(a.warmup + s)
+        for st, ev in zip(streams, ends):
+            ev.record(st)
+            main.wait_event(ev)
+        e1.record(main)
+        torch.cuda.synchronize(dev)
+    R.barrier()
+    ms = R.max(e0.elapsed_time(e1))
+    assert V.lib().vela_device_error(1) == 0, "a kernel reported a device error"
+    # the device-resident path computes what the host path computes
+    dev_ok = bool(np.array_equal(out[0].cpu().numpy(), lanes[0].run(seeds[0, a.warmup + a.steps - 1].cpu().numpy())))
+    per_step = a.lanes * a.batch
+    value = R.world * per_step * a.steps / (ms / 1000.0)
+
+    e2e = None
+    if not a.no_e2e:
+        host = [[seed_block(R.rank, l, 10_000 + s, a.batch) for s in range(a.steps + a.warmup)] for l in range(a.lanes)]
+        outs = [np.empty((a.batch, 32768), np.uint8) for _ in lanes]
+
+        def lane_loop(l, first, count):
+            e = lanes[l]
+            e.submit(host[l][first])
+            for i in range(count):
+                if i + 1 < count:
+                    e.submit(host[l][first + i + 1])
+                e.collect(outs[l])
+
+        def run_threads(first, count):
+            th = [threading.Thread(target=lane_loop, args=(l, first, count)) for l in range(a.lanes)]
+            for t in th:
+                t.start()
+            for t in th:
+                t.join()
+
+        run_threads(0, a.warmup)
+        R.barrier(); torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        run_threads(a.warmup, a.steps)
+        torch.cuda.synchronize(dev)
+        sec = R.max(time.perf_counter() - t0)
+        R.barrier()
+        e2e = {"value": R.world * per_step * a.steps / sec, "unit": UNIT,
+               "h2d_bytes_per_step": per_step * 32, "d2h_bytes_per_step": per_step * 32768,
+               "bytes_scope": "per GPU per step (seeds in, x0 out)", "timing": "host wall clock between barriers, max over ranks"}
+
+    roof = None
+    if not a.no_roofline:
+        case = AttentionCase(dev)
+        ams = case.time_ms()
+        hbm, bf16, src = peaks()
+        peak = 2.0 * bf16
+        achieved = ATTN_OPS / (ams / 1000.0) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "traffic": profile_traffic(), "kernel": "attn_kernel (vela_fused_attention), self-attention 8 x 5 heads x 4096 x 64",
+                "ms_per_launch": round(ams, 3), "ops_per_launch": ATTN_OPS,
+                "peak_note": f"int8 dense ops/s = 2 x the {src} bf16 burst GEMM rate; ops are single-pass algorithmic (the exact "
+                             f"3-pass algorithm executes the QK products twice more)"}
+        del case
+
+    cpu = None
+    if R.world == 1 and R.rank == 0 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(path)
+
+    for e in lanes:
+        e.close()
+    model.close()
+    if R.rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": R.world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 MMA / int32-int64", "data": "synthetic: seeded random-init int8 POISD model, ChaCha20 noise from per-(gpu, lane, step) seeds",
+                "config": {"workload": "one SD-turbo UNet denoising step (noise -> UNet -> x0) per inference, batch 8 x 2 lanes per GPU, "
+                                       "one CUDA graph per lane step", "batch": a.batch, "lanes": a.lanes, "inferences_per_step_per_gpu": per_step,
+                           "prompt_tokens": PROMPT, "l2": "inputs larger than L2: 1.4 GB of weights and ~2 GB of activations stream per step"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": kernels_per_step * a.steps * R.world, "kernels_per_step_per_gpu": kernels_per_step,
+                "clocks": clk.summary(), "x0_matches_reference_engine": ref_ok, "x0_same_on_all_ranks": same, "device_path_matches_host_path": dev_ok}
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(a, R):
+    import ctypes
+    import torch
+    so = os.path.join(ROOT, "oracle", "_ref", "libvela_ref.so")
+    if not os.path.exists(so):
+        if R.rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libvela_ref.so (the reference built from its sources) is missing; "
+                                                                  "build it with `make -C oracle ref` where the reference checkout is present"}), flush=True)
+        return
+    path = model_file(R.rank)
+    L = ctypes.CDLL(so)
+    L.ref_open.restype = ctypes.c_void_p
+    L.ref_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.ref_set_prompt.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    L.ref_bench.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]
+    L.ref_close.argtypes = [ctypes.c_void_p]
+    L.ref_last_error.restype = ctypes.c_char_p
+    h = L.ref_open(path.encode(), R.local, a.batch, a.lanes, 1)
+    if not h:
+        raise RuntimeError("reference engine: " + L.ref_last_error().decode())
+    toks = (ctypes.c_int * len(PROMPT))(*PROMPT)
+    if L.ref_set_prompt(h, toks, len(PROMPT)) != 0:
+        raise RuntimeError("reference set_prompt: " + L.ref_last_error().decode())
+    sec, inf = ctypes.c_double(), ctypes.c_longlong()
+    # warm-up inside ref_bench (two batches per lane per warm-up step); then K steps per lane, one host thread per lane
+    R.barrier(); torch.cuda.synchronize()
+    with Clocks(R.local) as clk:
+        if L.ref_bench(h, a.warmup, a.steps, ctypes.byref(sec), ctypes.byref(inf)) != 0:
+            raise RuntimeError("reference bench: " + L.ref_last_error().decode())
+    R.barrier()
+    s = R.max(sec.value)
+    L.ref_close(h)
+    if R.rank == 0:
+        per_step = a.lanes * a.batch
+        value = R.world * per_step * a.steps / s
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": R.world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": round(s * 1000.0 / a.steps, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 MMA / int32-int64", "data": "synthetic: the same seeded random-init int8 POISD model and prompt",
+                "config": {"workload": "one SD-turbo UNet denoising step (noise -> UNet -> x0) per inference, batch 8 x 2 lanes per GPU, "
+                                       "one CUDA graph per lane step", "batch": a.batch, "lanes": a.lanes, "inferences_per_step_per_gpu": per_step,
+                           "prompt_tokens": PROMPT, "l2": "inputs larger than L2: 1.4 GB of weights and ~2 GB of activations stream per step"},
+                "impl": "reference",
+                "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": a.lanes, "kind": "reference",
+                                 "sample": f"the reference engine compiled from its own sources for sm_100 (oracle/_ref/libvela_ref.so): "
+                                           f"Engine::submit/collect from {a.lanes} host threads per GPU (src/main.cpp:111-162), "
+                                           f"{a.steps} steps per lane after {a.warmup} warm-up steps; it runs on the GPU, the host threads only drive it"},
+                "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": per_step * 32, "d2h_bytes_per_step": per_step * 32768},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
+def run_kernel(a, R):
+    import torch
+    case = AttentionCase(torch.device("cuda", R.local))
+    for _ in range(3):
+        case.launch()
+    torch.cuda.synchronize()
+    assert case.L.vela_device_error(1) == 0
+
+
+def main():
+    a = parse()
+    R = Ranks()
+    R.init()
+    try:
+        if a.kernel:
+            run_kernel(a, R)
+        elif a.impl == "reference":
+            run_reference(a, R)
+        else:
+            run_vela(a, R)
+    finally:
+        R.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -180,6 +180,13 @@ int vela_engine_submit(vela_engine* e, const uint8_t* seeds);
 int vela_engine_collect(vela_engine* e, uint8_t* x0);
 /* one eager step handing every block output (host int32) to `tap` in UNet order (no reference counterpart: parity taps). */
 int vela_engine_step_taps(vela_engine* e, const uint8_t* seeds, uint8_t* x0, vela_tap_fn tap, void* user);
+/* Device-resident form of one step (no reference counterpart: the reference's forwardIO always copies the seeds
+ * from and x0 to pinned host memory, src/engine.cu:599-609).  d_seeds [batch][32] and d_x0 [batch][32768] are
+ * device pointers on the engine's device.  The step is enqueued on vela_engine_stream() and the call returns
+ * without waiting; the first call captures its CUDA graph. */
+int vela_engine_launch_device(vela_engine* e, const uint8_t* d_seeds, uint8_t* d_x0);
+/* kernel nodes in the engine's last captured step graph (0 before the first capture; no reference counterpart) */
+int vela_engine_graph_kernels(const vela_engine* e);
 int vela_engine_in_flight(const vela_engine* e);
 int vela_engine_batch(const vela_engine* e);
 size_t vela_engine_arena_peak(const vela_engine* e);

@@ -124,6 +124,19 @@ class Engine:
                                           ctypes.cast(cb, ctypes.c_void_p), None))
         return x0
 
+    def launch_device(self, d_seeds, d_x0):
+        """enqueue one step on device-resident seeds / x0 (device addresses as ints); returns without waiting"""
+        check(lib().vela_engine_launch_device(self.h, ctypes.c_void_p(d_seeds), ctypes.c_void_p(d_x0)))
+
+    @property
+    def stream(self):
+        """the engine's cudaStream_t, as an int"""
+        return lib().vela_engine_stream(self.h) or 0
+
+    @property
+    def graph_kernels(self):
+        return lib().vela_engine_graph_kernels(self.h)
+
     @property
     def last_ms(self):
         return lib().vela_engine_last_ms(self.h)

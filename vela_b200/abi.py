@@ -68,6 +68,8 @@ SIGNATURES = {
     "vela_engine_submit": (I, [P, P]),
     "vela_engine_collect": (I, [P, P]),
     "vela_engine_step_taps": (I, [P, P, P, P, P]),
+    "vela_engine_launch_device": (I, [P, P, P]),
+    "vela_engine_graph_kernels": (I, [P]),
     "vela_engine_in_flight": (I, [P]),
     "vela_engine_batch": (I, [P]),
     "vela_engine_arena_peak": (SZ, [P]),

@@ -237,6 +237,7 @@ public:
     ~Engine() {
         cudaSetDevice(m_.device);
         if (st_) cudaStreamSynchronize(st_);
+        if (gexec_dev_) cudaGraphExecDestroy(gexec_dev_);
         for (int s = 0; s < 2; ++s) { if (gexec_[s]) cudaGraphExecDestroy(gexec_[s]); if (done_[s]) cudaEventDestroy(done_[s]); if (hSeeds_[s]) cudaFreeHost(hSeeds_[s]); if (hOut_[s]) cudaFreeHost(hOut_[s]); }
         for (void* p : persist_) cudaFree(p);
         if (ev0_) cudaEventDestroy(ev0_); if (ev1_) cudaEventDestroy(ev1_);
@@ -338,6 +339,18 @@ public:
         std::memcpy(x0, hOut_[slot], size_t(32768) * B_);
         col_slot_ ^= 1; --inflight_;
     }
+    // ---- device-resident form: seeds and x0 in device memory, enqueued on st_ without waiting (slot 0's buffers)
+    void launch_device(const uint8_t* dseeds, uint8_t* dx0) {
+        VELA_REQUIRE(have_prompt_, "launch_device: no prompt set");
+        VELA_REQUIRE(inflight_ == 0, "launch_device: batches in flight (collect them first)");
+        VELA_CUDA(cudaSetDevice(m_.device));
+        if (graph_ && !gexec_dev_) gexec_dev_ = capture(0, false);
+        VELA_CUDA(cudaMemcpyAsync(dSeeds_[0], dseeds, size_t(32) * B_, cudaMemcpyDeviceToDevice, st_));
+        if (graph_) VELA_CUDA(cudaGraphLaunch(gexec_dev_, st_));
+        else forward(0, false);
+        VELA_CUDA(cudaMemcpyAsync(dx0, dOut_[0], size_t(32768) * B_, cudaMemcpyDeviceToDevice, st_));
+    }
+    int graph_kernels() const { return graph_kernels_; }
     // ---- one eager step with every block output handed to `tap` (parity against the reference's blocks)
     void step_taps(const uint8_t* seeds, uint8_t* x0, TapFn tap, void* user) {
         VELA_REQUIRE(have_prompt_, "step_taps: no prompt set");
@@ -357,6 +370,7 @@ private:
     cudaStream_t st_ = nullptr; Arena arena_; std::vector<void*> persist_;
     uint8_t *dSeeds_[2] = {nullptr, nullptr}, *dOut_[2] = {nullptr, nullptr}, *hSeeds_[2] = {nullptr, nullptr}, *hOut_[2] = {nullptr, nullptr};
     cudaGraphExec_t gexec_[2] = {nullptr, nullptr}; bool ready_[2] = {false, false};
+    cudaGraphExec_t gexec_dev_ = nullptr; int graph_kernels_ = 0;
     cudaEvent_t done_[2] = {nullptr, nullptr}, ev0_ = nullptr, ev1_ = nullptr;
     int inflight_ = 0, sub_slot_ = 0, col_slot_ = 0;
     int32_t *dNoise_ = nullptr, *dX_ = nullptr, *dEps_ = nullptr, *dIds_ = nullptr, *dCtx_ = nullptr;
@@ -650,8 +664,9 @@ private:
         lnorm(st_, x.d, T, D, fn.g64, fn.beta64, fn.den, dCtx_);
     }
     // Engine::forwardIO (src/engine.cu:599-609)
-    void forward(int slot) {
-        VELA_CUDA(cudaMemcpyAsync(dSeeds_[slot], hSeeds_[slot], size_t(32) * B_, cudaMemcpyHostToDevice, st_));
+    // io = false: the step reads dSeeds_[slot] and leaves x0 in dOut_[slot] (device-resident form, launch_device)
+    void forward(int slot, bool io = true) {
+        if (io) VELA_CUDA(cudaMemcpyAsync(dSeeds_[slot], hSeeds_[slot], size_t(32) * B_, cudaMemcpyHostToDevice, st_));
         arena_.off = 0;
         workspace_ = arena_.alloc(WORKSPACE);
         noise(st_, dSeeds_[slot], B_, nullptr, m_.lut_gauss, m_.c_cin, dNoise_, dX_);
@@ -660,22 +675,33 @@ private:
         Tensor eps; eps.d = dEps_; eps.B = B_; eps.T = 4096; eps.C = 4;
         unet(x, eps);
         finalize(st_, dNoise_, dEps_, B_, m_.c_sig, dOut_[slot]);
-        VELA_CUDA(cudaMemcpyAsync(hOut_[slot], dOut_[slot], size_t(32768) * B_, cudaMemcpyDeviceToHost, st_));
+        if (io) VELA_CUDA(cudaMemcpyAsync(hOut_[slot], dOut_[slot], size_t(32768) * B_, cudaMemcpyDeviceToHost, st_));
+    }
+    cudaGraphExec_t capture(int slot, bool io) {
+        forward(slot, io);
+        VELA_CUDA(cudaStreamSynchronize(st_));
+        VELA_CUDA(cudaGetLastError());
+        cudaGraph_t g = nullptr;
+        VELA_CUDA(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
+        try { forward(slot, io); } catch (...) { cudaStreamEndCapture(st_, &g); if (g) cudaGraphDestroy(g); throw; }
+        VELA_CUDA(cudaStreamEndCapture(st_, &g));
+        size_t n = 0;
+        VELA_CUDA(cudaGraphGetNodes(g, nullptr, &n));
+        std::vector<cudaGraphNode_t> nodes(n);
+        VELA_CUDA(cudaGraphGetNodes(g, nodes.data(), &n));
+        int kernels = 0;
+        for (size_t i = 0; i < n; ++i) { cudaGraphNodeType t; VELA_CUDA(cudaGraphNodeGetType(nodes[i], &t)); kernels += t == cudaGraphNodeTypeKernel; }
+        graph_kernels_ = kernels;
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t rc = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        VELA_CUDA(rc);
+        return ex;
     }
     // graph per slot: one eager warm-up run, then capture (src/engine.cu:610-631)
     void ensure_slot(int slot) {
         if (ready_[slot]) return;
-        if (graph_) {
-            forward(slot);
-            VELA_CUDA(cudaStreamSynchronize(st_));
-            VELA_CUDA(cudaGetLastError());
-            cudaGraph_t g;
-            VELA_CUDA(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
-            try { forward(slot); } catch (...) { cudaStreamEndCapture(st_, &g); if (g) cudaGraphDestroy(g); throw; }
-            VELA_CUDA(cudaStreamEndCapture(st_, &g));
-            VELA_CUDA(cudaGraphInstantiate(&gexec_[slot], g, 0));
-            cudaGraphDestroy(g);
-        }
+        if (graph_) gexec_[slot] = capture(slot, true);
         ready_[slot] = true;
     }
     void launch(int slot) {
@@ -729,6 +755,10 @@ extern "C" int vela_engine_collect(vela_engine* e, uint8_t* x0) {
 extern "C" int vela_engine_step_taps(vela_engine* e, const uint8_t* seeds, uint8_t* x0, vela_tap_fn tap, void* user) {
     return guarded("vela_engine_step_taps", [&] { VELA_REQUIRE(e && seeds && x0, "bad arguments"); e->e->step_taps(seeds, x0, tap, user); });
 }
+extern "C" int vela_engine_launch_device(vela_engine* e, const uint8_t* d_seeds, uint8_t* d_x0) {
+    return guarded("vela_engine_launch_device", [&] { VELA_REQUIRE(e && d_seeds && d_x0, "bad arguments"); e->e->launch_device(d_seeds, d_x0); });
+}
+extern "C" int vela_engine_graph_kernels(const vela_engine* e) { return e ? e->e->graph_kernels() : 0; }
 extern "C" int vela_engine_in_flight(const vela_engine* e) { return e ? e->e->in_flight() : 0; }
 extern "C" int vela_engine_batch(const vela_engine* e) { return e ? e->e->batch() : 0; }
 extern "C" size_t vela_engine_arena_peak(const vela_engine* e) { return e ? e->e->arena_peak() : 0; }
