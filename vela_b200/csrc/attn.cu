@@ -47,9 +47,10 @@ constexpr int OFF_V = OFF_K + KS * KSTAGE;
 constexpr int OFF_P = OFF_V + VS * VSTAGE;
 constexpr int OFF_KAUX = OFF_P + 2 * P_BYTES;          // per K stage: ek int32[64], ksum int64[64]
 constexpr int KAUX_BYTES = 64 * 4 + 64 * 8;
-constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1024]
-constexpr int OFF_RED = OFF_LUT + 1024 * 8;            // cross-warp reductions: 2 x 128 x 8 bytes
-constexpr int OFF_BAR = OFF_RED + 2 * 128 * 8;
+constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025]: (L[i], L[i+1] - L[i]); entry 1024 = (0, 0)
+constexpr int OFF_RED = OFF_LUT + 1032 * 8;            // cross-warp reductions: 2 x 128 x 8 bytes
+constexpr int OFF_WK = OFF_RED + 2 * 128 * 8;          // per softmax warp: ek[32], 128*ksum[32] of its keys
+constexpr int OFF_BAR = OFF_WK + 8 * 64 * 4;
 constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
 constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;
 constexpr int TMEM_COLS = 512;
@@ -70,23 +71,93 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
-// exact sat32(rshr(65536 hh + T, sh)) with a shift class that is uniform across the warp:
-// 0: every sh >= 16, 1: every sh in [5, 15], 2: anything else (64-bit path)
-__device__ __forceinline__ int score_c(int hh, int T, int sh, int cls) {
-    if (cls == 0) return (hh + ((T + (1 << (sh - 1))) >> 16)) >> (sh - 16);
-    if (cls == 1) {       // floor((hh 2^16 + T + 2^(sh-1)) / 2^sh) = hh 2^(16-sh) + rshr(T, sh); the sum fits int32 (|S| < 2^37, sh >= 5)
-        const int t = ((T >> (sh - 1)) + 1) >> 1;
-        return int(uint32_t(hh) << (16 - sh)) + t;
-    }
-    return int(rshr((i64(hh) << 16) + T, sh));
+// s = sat32(rshr(65536 hh + T, sh)) for a shift sh in [5, 19], T = 256 xx + ll + cq + 128 ksum + 2^(sh-1) (the
+// rounding term already added).  |S| < 2^36 (64 products of 16-bit values), so S fits 64 bits, S / 2^5 fits 32 bits
+// and no saturation can occur: one wide multiply-add and one funnel shift of the 64-bit sum.
+__device__ __forceinline__ int score_fast(int hh, int T, int sh) {
+    const long long S = (long long)hh * 65536 + T;
+    return int(__funnelshift_r(uint32_t(S), uint32_t(S >> 32), sh));
 }
 
-// E = expLUT(z) for z = mx - s >= 0; 0 from z = 2^20 on.  L2[i] = (L[i], L[i+1] - L[i]).
-__device__ __forceinline__ uint32_t lut_exp(uint32_t z, const int2* L2) {
-    const uint32_t zc = min(z, (16u << 16) - 1);
-    const int2 e = L2[zc >> 10];
-    const int v = e.x + int((i64(e.y) * int(zc & 1023)) >> 10);
-    return z < (16u << 16) ? uint32_t(v) : 0u;
+// E = expLUT(z) for z = mx - s >= 0 (z < 2^32): index min(z >> 10, 1024), the sentinel entry 1024 = (0, 0) giving
+// E = 0 from z = 2^20 on; linear interpolation over the low 10 bits.
+__device__ __forceinline__ int lut_exp(uint32_t z, const int2* L2) {
+    const int2 e = L2[min(z >> 10, 1024u)];
+    return e.x + int(((long long)e.y * int(z & 1023u)) >> 10);
+}
+
+// One 32-key half tile of one pass for one query row (this thread) -- scores from the three TMEM accumulators
+// (HH at taddr, X at +64, LL at +128), then PASS 0: row max; PASS 1: sum of E; PASS 2: P (into pw_h / pw_l).
+template <int PASS>
+__device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ wk, int shq, int r0, int cq, bool fast, bool full,
+                                             int kbase, int q, int Tk, int causal, const int2* __restrict__ L2,
+                                             int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l) {
+    #pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        int hh[16], xx[16], ll[16];
+        tmem_ld16(taddr + c * 16, hh); tmem_ld16(taddr + c * 16 + 64, xx); tmem_ld16(taddr + c * 16 + 128, ll);
+        tmem_ld_wait();
+        int s[16];
+        if (fast) {
+            #pragma unroll
+            for (int u = 0; u < 16; u += 4) {
+                const int4 e4 = *reinterpret_cast<const int4*>(wk + c * 16 + u);
+                const int4 k4 = *reinterpret_cast<const int4*>(wk + 32 + c * 16 + u);
+                const int ek[4] = {e4.x, e4.y, e4.z, e4.w}, kc[4] = {k4.x, k4.y, k4.z, k4.w};
+                #pragma unroll
+                for (int w = 0; w < 4; ++w)
+                    s[u + w] = score_fast(hh[u + w], (xx[u + w] << 8) + ll[u + w] + (cq + kc[w]) + (r0 >> ek[w]), shq - ek[w]);
+            }
+        } else {            // a shift outside [5, 19] somewhere in the tile: the 64-bit rshr with saturation
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int ek = wk[c * 16 + u], kc = wk[32 + c * 16 + u];
+                s[u] = int(rshr((i64(hh[u]) << 16) + ((xx[u] << 8) + ll[u] + cq + kc), shq - ek));
+            }
+        }
+        uint32_t vmask = 0xFFFFu;   // validity by key position (a valid score may itself saturate to INT_MIN)
+        if (!full) {
+            vmask = 0;
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) { const int key = kbase + c * 16 + u; vmask |= uint32_t(key < Tk && !(causal && key > q)) << u; }
+        }
+        if constexpr (PASS == 0) {
+            if (!full) {
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) s[u] = (vmask >> u) & 1u ? s[u] : INT_MIN;
+            }
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
+        } else {
+            int E[16];
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) E[u] = lut_exp(uint32_t(mx) - uint32_t(s[u]), L2);
+            if (!full) {
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) E[u] = (vmask >> u) & 1u ? E[u] : 0;
+            }
+            if constexpr (PASS == 1) {
+                // each E < 2^31 (the table holds int32 values >= 0): a pair fits 32 bits
+                #pragma unroll
+                for (int u = 0; u < 16; u += 2) sum += uint32_t(E[u]) + uint32_t(E[u + 1]);
+            } else {
+                // P = min(32767, (E r + 2^46) >> 47) with r = rhi 2^32 + rlo.  E <= sum E, so E r <= 2^62 and
+                // floor(E r / 2^32) = E rhi + umulhi(E, rlo) <= 2^30 fits 32 bits.
+                int P[16];
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const uint32_t h = uint32_t(E[u]) * rhi + __umulhi(uint32_t(E[u]), rlo);
+                    P[u] = int(min(32767u, (h + 16384u) >> 15));
+                    psum += P[u];
+                }
+                #pragma unroll
+                for (int u = 0; u < 16; u += 4) {
+                    pw_h[c * 4 + u / 4] = pack_hi4(P[u], P[u + 1], P[u + 2], P[u + 3]);
+                    pw_l[c * 4 + u / 4] = pack_lo4(P[u], P[u + 1], P[u + 2], P[u + 3]);
+                }
+            }
+        }
+    }
 }
 
 __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ AttnArgs a) {
@@ -115,7 +186,10 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x) { const int x0 = __ldg(a.lexp + i), x1 = __ldg(a.lexp + i + 1); lut2[i] = make_int2(x0, x1 - x0); }
+    for (int i = threadIdx.x; i <= 1024; i += blockDim.x) {
+        if (i < 1024) { const int x0 = __ldg(a.lexp + i), x1 = __ldg(a.lexp + i + 1); lut2[i] = make_int2(x0, x1 - x0); }
+        else lut2[i] = make_int2(0, 0);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -208,105 +282,68 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         const size_t rq = size_t(g) * a.Tqp + q;
         const int eqv = __ldg(a.eq + rq);
         const int cq = int(32768 * __ldg(a.qhs + rq) + 128 * __ldg(a.qls + rq));
-        const int shq = 19 - eqv;
+        const int shq = 19 - eqv;                                   // eq <= 17, so shq >= 2
+        const int r0 = 1 << (shq - 1);                              // rounding term of shift shq; >> ek gives that of shq - ek
+        const int shq_min = __reduce_min_sync(0xffffffffu, shq);
+        int* wk = reinterpret_cast<int*>(sm + OFF_WK) + (warp - 2) * 64;
         i64* red = reinterpret_cast<i64*>(sm + OFF_RED);          // [2][128]
         int mx = INT_MIN; uint64_t sum = 0; uint32_t rlo = 0, rhi = 0; int psum = 0;
         int uses[2] = {0, 0};
         bool ok = true;
-        // Every warp runs all nIt iterations and every named barrier, also after a timed-out wait
+        // Every warp runs all iterations and every named barrier, also after a timed-out wait
         // (then it skips the work), so no warp can be left waiting on a barrier the others skipped.
-        for (int it = 0; it < nIt; ++it) {
-            const int pass = it / nT, j = it % nT, ks = it % KS;
-            const int b = pass < 2 ? (it & 1) : 0;
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], uses[b] & 1, a.err, DEVERR_TIMEOUT_FULL));
-            ++uses[b];
-            if (ok) {
-            tc_fence_after();
-            const int32_t* ekp = reinterpret_cast<const int32_t*>(sm + OFF_KAUX + ks * KAUX_BYTES) + half * 32;
-            const i64* ksp = reinterpret_cast<const i64*>(sm + OFF_KAUX + ks * KAUX_BYTES + 256) + half * 32;
-            const int kbase = j * 64 + half * 32;
-            const bool full = !a.causal && (j * 64 + 64 <= a.Tk);
-            uint32_t pw_h[8], pw_l[8];                            // P bytes of this thread's 32 keys (pass 2)
-            #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                int hh[16], xx[16], ll[16];
-                const uint32_t col = uint32_t(b * 192 + half * 32 + c * 16);
-                tmem_ld16(tmem + tl + col, hh); tmem_ld16(tmem + tl + col + 64, xx); tmem_ld16(tmem + tl + col + 128, ll);
-                tmem_ld_wait();
-                int ekk[16], kc[16];
-                int ekmin = INT_MAX, ekmax = INT_MIN;
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) { ekk[u] = ekp[c * 16 + u]; kc[u] = int(128 * ksp[c * 16 + u]); ekmin = min(ekmin, ekk[u]); ekmax = max(ekmax, ekk[u]); }
-                const int shmin = shq - ekmax, shmax = shq - ekmin;
-                const int cls = __all_sync(0xffffffffu, shmin >= 16) ? 0 : (__all_sync(0xffffffffu, shmin >= 5 && shmax <= 15) ? 1 : 2);
-                int s[16];
-                uint32_t vmask = 0;          // validity by key position (a valid score may itself saturate to INT_MIN)
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const int T = (xx[u] << 8) + ll[u] + cq + kc[u];
-                    const int key = kbase + c * 16 + u;
-                    const bool valid = full || (key < a.Tk && !(a.causal && key > q));
-                    vmask |= uint32_t(valid) << u;
-                    s[u] = valid ? score_c(hh[u], T, shq - ekk[u], cls) : INT_MIN;
-                }
-                if (pass == 0) {
-                    #pragma unroll
-                    for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
-                } else {
-                    #pragma unroll
-                    for (int u = 0; u < 16; u += 2) {
-                        const uint32_t e0 = (vmask >> u) & 1u ? lut_exp(uint32_t(mx) - uint32_t(s[u]), lut2) : 0u;
-                        const uint32_t e1 = (vmask >> (u + 1)) & 1u ? lut_exp(uint32_t(mx) - uint32_t(s[u + 1]), lut2) : 0u;
-                        if (pass == 1) sum += uint64_t(e0 + e1);            // each E <= 2^30: a pair fits 32 bits
-                        else {
-                            const uint32_t ev2[2] = {e0, e1};
-                            int pv2[2];
-                            #pragma unroll
-                            for (int w = 0; w < 2; ++w) {
-                                const uint64_t hi64 = uint64_t(ev2[w]) * rhi + __umulhi(ev2[w], rlo);
-                                pv2[w] = int(min(uint64_t(32767), (hi64 + (1u << 14)) >> 15));
-                            }
-                            psum += pv2[0] + pv2[1];
-                            s[u] = pv2[0]; s[u + 1] = pv2[1];           // reuse: P values
-                        }
-                    }
-                    if (pass == 2) {
-                        #pragma unroll
-                        for (int u = 0; u < 16; u += 4) {
-                            pw_h[c * 4 + u / 4] = pack_hi4(s[u], s[u + 1], s[u + 2], s[u + 3]);
-                            pw_l[c * 4 + u / 4] = pack_lo4(s[u], s[u + 1], s[u + 2], s[u + 3]);
-                        }
-                    }
-                }
-            }
-            // this warp is done with the QK buffer and the K stage's per-key data
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) { mbar_arrive(&qk_free[b]); mbar_arrive(&k_empty[ks]); }
-            if (pass == 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
+        for (int pass = 0; pass < 3; ++pass) {
+            for (int j = 0; j < nT; ++j) {
+                const int it = pass * nT + j, ks = it % KS;
+                const int b = pass < 2 ? (it & 1) : 0;
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], uses[b] & 1, a.err, DEVERR_TIMEOUT_FULL));
+                ++uses[b];
                 if (ok) {
-                uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
-                *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
-                *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_h[4], pw_h[5], pw_h[6], pw_h[7]);
-                *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2)) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
-                *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_l[4], pw_l[5], pw_l[6], pw_l[7]);
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(p_full);
+                    tc_fence_after();
+                    // this warp's 32 keys: exponent and 128 * ksum, staged once per tile for vector reads
+                    const uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
+                    const int ekL = reinterpret_cast<const int32_t*>(aux)[half * 32 + lane];
+                    const int kcL = int(128 * reinterpret_cast<const i64*>(aux + 256)[half * 32 + lane]);
+                    const int emax = __reduce_max_sync(0xffffffffu, ekL);
+                    wk[lane] = ekL; wk[32 + lane] = kcL;
+                    __syncwarp();
+                    const int kbase = j * 64 + half * 32;
+                    const bool full = !a.causal && kbase + 32 <= a.Tk;
+                    const bool fast = shq_min - emax >= 5;           // every shift of the tile in [5, 19]
+                    const uint32_t taddr = tmem + tl + uint32_t(b * 192 + half * 32);
+                    uint32_t pw_h[8], pw_l[8];                        // P bytes of this thread's 32 keys (pass 2)
+                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    // this warp is done with the QK buffer, the K stage's per-key data and its key staging
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) { mbar_arrive(&qk_free[b]); mbar_arrive(&k_empty[ks]); }
+                    if (pass == 2) {
+                        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
+                        if (ok) {
+                            uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
+                            *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
+                            *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_h[4], pw_h[5], pw_h[6], pw_h[7]);
+                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2)) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
+                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_l[4], pw_l[5], pw_l[6], pw_l[7]);
+                            fence_async_smem();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(p_full);
+                        }
+                    }
                 }
-            }
-            }
-            if (j == nT - 1 && pass < 2) {         // combine the two key halves of each row
-                red[half * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                const i64 other = red[(half ^ 1) * 128 + rl];
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                if (pass == 0) mx = max(mx, int(other));
-                else {
-                    const uint64_t tot = sum + uint64_t(other);
-                    const uint64_t r = tot ? (uint64_t(1) << 62) / tot : 0;
-                    rlo = uint32_t(r); rhi = uint32_t(r >> 32);
+                if (j == nT - 1 && pass < 2) {         // combine the two key halves of each row
+                    red[half * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
+                    const i64 other = red[(half ^ 1) * 128 + rl];
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
+                    if (pass == 0) mx = max(mx, int(other));
+                    else {
+                        const uint64_t tot = sum + uint64_t(other);
+                        const uint64_t r = tot ? (uint64_t(1) << 62) / tot : 0;
+                        rlo = uint32_t(r); rhi = uint32_t(r >> 32);
+                    }
                 }
             }
         }
