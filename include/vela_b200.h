@@ -131,6 +131,14 @@ int vela_quant_heads(void* stream, const int32_t* X, int B, int T, int C, int he
 int vela_quant_heads_pad(void* stream, int G, int T, int Tp, int8_t* hi, int8_t* lo, int32_t* e, int64_t* hs, int64_t* ls, int64_t* tsum);
 /* V column quantisation, transposed [G, 64, Tkp] + ev, vsum; scratch u32[G*64].  k_quant_v (src/kernels.h:49-50). */
 int vela_quant_v(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum, uint32_t* scratch);
+/* vela_quant_v for callers that must not allocate device memory (no counterpart in the reference): the same
+ * outputs, with the column-max scratch in a library-owned static device array of VELA_QUANT_V_STATIC_MAX_COLS
+ * words (256 KiB per GPU, held until exit) instead of a caller buffer.  Requires B*heads*64 <= that maximum
+ * (VELA_ERR_ARG otherwise).  The first call on a device looks up the array's device address; make it before any
+ * stream capture.  All calls on a device share the array: calls that overlap on the GPU race, so order them on
+ * one stream. */
+#define VELA_QUANT_V_STATIC_MAX_COLS 65536
+int vela_quant_v_static(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum);
 
 /* ---------------------------------------------------------------------------------
  * Exact integer attention on the tensor cores.

@@ -56,6 +56,7 @@ SIGNATURES = {
     "vela_quant_heads": (I, [P, P, I, I, I, I, I, P, P, P, P, P, P]),
     "vela_quant_heads_pad": (I, [P, I, I, I, P, P, P, P, P, P]),
     "vela_quant_v": (I, [P, P, I, I, I, I, I, P, P, P, P, P]),
+    "vela_quant_v_static": (I, [P, P, I, I, I, I, I, P, P, P, P]),
     "vela_fused_attention": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, P, P]),
     "vela_model_load": (P, [I, ctypes.c_char_p]),
     "vela_model_free": (None, [P]),
