@@ -144,6 +144,37 @@ def test_conv_320ch_16x16():
         assert np.array_equal(got, exp), stride
 
 
+@pytest.mark.parametrize("B,Hh,C,N", [(2, 12, 64, 128), (3, 8, 96, 64), (1, 32, 64, 192)])
+def test_conv_shapes_both_loaders(B, Hh, C, N):
+    """image sizes whose 128-row tiles are not whole output rows (12x12, stride-2 6x6) keep the per-thread loader;
+    8x8 (whole images per tile, odd batch) and 32x32 (whole rows) stage the image by TMA"""
+    rng = np.random.default_rng(B * 100 + Hh); d = Dev()
+    X = rbits(rng, (B, Hh, Hh, C), 24)
+    W = rng.integers(-127, 128, (N, 9 * C)).astype(np.int8)
+    c = cst_for(rng, W, N, N)
+    for stride in (1, 2):
+        got, exp = conv_case(d, X, W, c, stride)
+        assert np.array_equal(got, exp), (B, Hh, C, N, stride)
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 96, 128), (130, 160, 64)])
+def test_x32_ragged_k(M, K, N):
+    """int32 source whose K is not a multiple of 64: the staged box past K reads zeros (quantised value 0)"""
+    rng = np.random.default_rng(M + K); d = Dev()
+    Kp = (K + 15) // 16 * 16; Mp = (M + 63) // 64 * 64
+    X = rbits(rng, (M, K), 28)
+    W = rng.integers(-127, 128, (N, Kp)).astype(np.int8); c = cst_for(rng, W, N, N)
+    rowmax = np.abs(X.astype(np.int64)).max(1).astype(np.uint32)
+    a = abi.ASrc(); a.src = abi.SRC_X32; a.x = A(d(X)); a.ldx = K; a.K = K; a.rowmax = A(d(rowmax.view(np.int32)))
+    Y = d.empty((M, N), torch.int32, 0x5A)
+    E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = A(Y); E.ldy = N
+    run_gemm(a, Mp, M, d(W), Kp, N, N, Kp, d(c), E)
+    hi, lo, e = O.quant_rows(X, Kp, Mp)
+    exp = np.zeros((M, N), np.int32)
+    O.gemm_hl(hi, lo, M, W, N, Kp, c, e, O.EPI_PLAIN, Y=exp, ldy=N)
+    assert np.array_equal(H(Y), exp)
+
+
 def test_config1_shape():
     """config 1: A 16-bit uniform over [-32768, 32767] as planes, M 4096, N = K = 320, e in [0, 12)."""
     rng = np.random.default_rng(1); d = Dev()

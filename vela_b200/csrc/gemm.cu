@@ -43,16 +43,18 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 // the instantiations live in gemm_inst_*.cu
 #define VELA_GEMM_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm<BN, ST, SRC, EPI>(const GemmArgs&, int, cudaStream_t);
 VELA_GEMM_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_PLAIN)
-VELA_GEMM_EXTERN(64, 6, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_X32, EPI_PLAIN)
-VELA_GEMM_EXTERN(64, 6, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_CONV32, EPI_PLAIN)
+VELA_GEMM_EXTERN(64, 3, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 3, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 3, SRC_X32, EPI_PLAIN)
+VELA_GEMM_EXTERN(64, 3, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 3, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 3, SRC_CONV32, EPI_PLAIN)
 VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_GEGLU) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_GEGLU)
 VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_SPLIT3) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_QKV)
 
 namespace {
+// int32 sources run a 3-stage MMA ring: the TMA staging ring of the raw operand holds the prefetch depth
 template <int SRC> void dispatch_plain(int BN, const GemmArgs& a, int splits, cudaStream_t st) {
-    if (BN == 64) launch_gemm<64, 6, SRC, EPI_PLAIN>(a, splits, st);
-    else if (BN == 128) launch_gemm<128, 4, SRC, EPI_PLAIN>(a, splits, st);
-    else launch_gemm<256, 4, SRC, EPI_PLAIN>(a, splits, st);
+    constexpr int S64 = SRC == SRC_I8 ? 6 : 3, S = SRC == SRC_I8 ? 4 : 3;
+    if (BN == 64) launch_gemm<64, S64, SRC, EPI_PLAIN>(a, splits, st);
+    else if (BN == 128) launch_gemm<128, S, SRC, EPI_PLAIN>(a, splits, st);
+    else launch_gemm<256, S, SRC, EPI_PLAIN>(a, splits, st);
 }
 }  // namespace
 
@@ -103,11 +105,29 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
         VELA_REQUIRE(A.x && A.rowmax && A.K > 0 && A.K % 32 == 0 && A.K <= Kp && A.ldx >= A.K && A.ldx % 4 == 0, "gemm: int32 source needs K % 32 == 0, ldx % 4 == 0");
         VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.x) & 15) == 0, "gemm: int32 source must be 16-byte aligned");
         a.x = A.x; a.ldx = A.ldx; a.rowmax_in = A.rowmax; a.K = A.K;
+        // staged by TMA: boxes of 128 rows x 32 int32 (128-byte rows, 128-byte swizzle), zeros past Mreal and K
+        a.tmX = tmap2d(A.x, CU_TENSOR_MAP_DATA_TYPE_INT32, uint64_t(A.K), uint64_t(Mreal), uint64_t(A.ldx) * 4, 32, 128, Swz::B128);
+        a.xtma = 1;
     } else if (src == VELA_SRC_CONV32) {
         VELA_REQUIRE(A.img && A.e && A.C % 32 == 0 && A.K == 9 * A.C && A.K <= Kp && A.stride >= 1, "gemm: conv source needs C % 32 == 0, K = 9C");
         VELA_REQUIRE(A.Ho == (A.H - 1) / A.stride + 1 && A.Wo == (A.W - 1) / A.stride + 1, "gemm: conv output size");
         VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.img) & 15) == 0, "gemm: image must be 16-byte aligned");
         a.img = A.img; a.H = A.H; a.W = A.W; a.C = A.C; a.stride = A.stride; a.Ho = A.Ho; a.Wo = A.Wo; a.K = A.K; a.e = A.e;
+        // Implicit im2col through TMA.  For tap (ky, kx) and 32 channels from c0, the 128 output pixels of a tile
+        // read the NHWC box starting at (c0, kx - 1, oy0*s + ky - 1, b0) with element strides (1, s, s, 1); the
+        // padding ring (coordinates -1 and past the edge) reads zeros.  Tiles must be whole output rows of one
+        // image (Ho*Wo % 128 == 0 and 128 % Wo == 0) or whole images (128 % (Ho*Wo) == 0); other shapes keep
+        // the per-thread loads.
+        const int howo = A.Ho * A.Wo, s = A.stride;
+        int bw = 0, bh = 0, bb = 0;
+        if (howo % 128 == 0 && 128 % A.Wo == 0) { bw = A.Wo * s; bh = (128 / A.Wo) * s; bb = 1; }
+        else if (128 % howo == 0) { bw = A.Wo * s; bh = A.Ho * s; bb = 128 / howo; }
+        if (bw > 0 && bw <= 256 && bh <= 256 && s <= 8) {
+            const int Bimg = ceil_div(Mreal, howo);
+            a.tmX = tmap_nhwc(A.img, uint64_t(Bimg), uint64_t(A.H), uint64_t(A.W), uint64_t(A.C), 32, uint32_t(bw), uint32_t(bh), uint32_t(bb),
+                              uint32_t(s), Swz::B128);
+            a.xtma = 1; a.conv_rows_per_img = howo;
+        }
     } else {
         throw Error(VELA_ERR_ARG, "gemm: unknown A source");
     }

@@ -37,6 +37,9 @@ enum { EPI_PLAIN = 0, EPI_SPLIT3 = 1, EPI_GEGLU = 2, EPI_GELU = 3, EPI_QKV = 4 }
 
 struct GemmArgs {
     CUtensorMap tmA_hi, tmA_lo, tmW;
+    CUtensorMap tmX;                                        // int32 sources staged by TMA (xtma = 1): X rows or the NHWC image
+    int xtma;                                               // 1: int32 operand through tmX + staging ring; 0: per-thread loads
+    int conv_rows_per_img;                                  // SRC_CONV32 with xtma: output rows per image (Ho*Wo)
     int Mreal, Nreal, Np, Mp, Kp, nkb, kb_per_split;
     const int32_t* e;                                       // SRC_I8 / SRC_CONV32: per-row exponent
     const int32_t* x; int ldx; const uint32_t* rowmax_in; int K;   // SRC_X32 (and K bound of int32 sources)
@@ -58,6 +61,14 @@ template <int BN, int STAGES> struct GemmCfg {
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
     static constexpr int CTRL = 1024;                        // barriers + TMEM slot
     static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE + CTRL + BN * 16 /*column constants*/;
+    // int32 staging ring (SRC_X32 / SRC_CONV32 through TMA): one k-block = two boxes of 128 rows x 32 int32
+    // (128-byte rows, 128-byte swizzle), as many stages as fit beside the MMA ring (at most 4)
+    static constexpr int X_HALF = BM * 128;
+    static constexpr int X_STAGE = 2 * X_HALF;
+    static constexpr int OFF_X = (STAGES * STAGE + CTRL + BN * 16 + 1023) / 1024 * 1024;
+    static constexpr int X_FIT = (227 * 1024 - 1024 - OFF_X) / X_STAGE;
+    static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
+    static constexpr int SMEM_X = 1024 + OFF_X + (X_STAGES > 0 ? X_STAGES : 0) * X_STAGE;
     static constexpr int THREADS = 320;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "MMA N");
     static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -73,7 +84,10 @@ __global__ void __launch_bounds__(320, 1) gemm_w8a16_kernel(const __grid_constan
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE);
     uint64_t* empty = full + STAGES;
     uint64_t* accb = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+    uint64_t* xfull = accb + 1;                      // int32 staging ring (xtma)
+    uint64_t* xempty = xfull + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 4);
+    uint8_t* xstage = smem + Cfg::OFF_X;
     int4* s_cst = reinterpret_cast<int4*>(smem + STAGES * Cfg::STAGE + Cfg::CTRL);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,12 +100,14 @@ __global__ void __launch_bounds__(320, 1) gemm_w8a16_kernel(const __grid_constan
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1 + (REG ? 8 : 0)); mbar_init(&empty[s], 1); }
         mbar_init(accb, 1);
+        for (int s = 0; s < 4; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], 8); }
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&a.tmW);
         if (SRC == SRC_I8) { tma_prefetch_desc(&a.tmA_hi); tma_prefetch_desc(&a.tmA_lo); }
+        if (REG && a.xtma) tma_prefetch_desc(&a.tmX);
     }
     tc_fence_before();
     __syncthreads();
@@ -101,11 +117,33 @@ __global__ void __launch_bounds__(320, 1) gemm_w8a16_kernel(const __grid_constan
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
+            int cb = 0, cy0 = 0;                     // SRC_CONV32 + xtma: image and first output row of this tile
+            if (SRC == SRC_CONV32 && a.xtma) { cb = m0 / a.conv_rows_per_img; cy0 = (m0 - cb * a.conv_rows_per_img) / a.Wo; }
             for (int i = 0; i < nk; ++i) {
                 const int s = i % STAGES; const uint32_t ph = (i / STAGES) & 1;
+                const int k = (kb0 + i) * Cfg::BK;
+                if constexpr (REG && Cfg::X_STAGES > 0) {
+                    if (a.xtma) {
+                        // stage the int32 operand of this k-block (zeros outside the matrix / image)
+                        const int xs = i % Cfg::X_STAGES;
+                        if (!mbar_wait(&xempty[xs], ((i / Cfg::X_STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
+                        mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
+                        #pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            uint8_t* dst = xstage + xs * Cfg::X_STAGE + hf * Cfg::X_HALF;
+                            const int kk = k + hf * 32;
+                            if (SRC == SRC_X32) tma_load_2d(dst, &a.tmX, &xfull[xs], kk, m0);
+                            else {
+                                const int tap = kk / a.C, c0 = kk - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
+                                // taps past the ninth (K padding) read a box wholly below the image: zeros
+                                const int yy = tap < 9 ? cy0 * a.stride + ky - 1 : a.H + 8;
+                                tma_load_4d(dst, &a.tmX, &xfull[xs], tap < 9 ? c0 : 0, kx - 1, yy, cb);
+                            }
+                        }
+                    }
+                }
                 if (!mbar_wait(&empty[s], ph ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
                 uint8_t* st = smem + s * Cfg::STAGE;
-                const int k = (kb0 + i) * Cfg::BK;
                 mbar_arrive_expect_tx(&full[s], Cfg::W_BYTES + (SRC == SRC_I8 ? 2 * Cfg::A_BYTES : 0));
                 tma_load_2d(st + 2 * Cfg::A_BYTES, &a.tmW, &full[s], k, n0);
                 if (SRC == SRC_I8) {
@@ -153,24 +191,40 @@ __global__ void __launch_bounds__(320, 1) gemm_w8a16_kernel(const __grid_constan
             }
             for (int i = 0; i < nk; ++i) {
                 const int s = i % STAGES; const uint32_t ph = (i / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
-                const int k = (kb0 + i) * Cfg::BK + half * 32;
-                const int32_t* src = nullptr;
-                if (live && k < a.K) {
-                    if (SRC == SRC_X32) src = a.x + size_t(grow) * a.ldx + k;
-                    else {
-                        const int tap = k / a.C, c0 = k - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
-                        const int iy = iy0 + ky, ix = ix0 + kx;
-                        if (iy >= 0 && iy < a.H && ix >= 0 && ix < a.W) src = a.img + ((size_t(cb) * a.H + iy) * a.W + ix) * a.C + c0;
+                int4 v[8];
+                bool staged = false;
+                if constexpr (Cfg::X_STAGES > 0) {
+                    if (a.xtma) {
+                        // this thread's 32 int32 from the staging ring (128-byte swizzle: chunk j at j ^ (row & 7))
+                        const int xs = i % Cfg::X_STAGES;
+                        if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (i / Cfg::X_STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL))) break;
+                        const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
+                        #pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&xempty[xs]);
+                        staged = true;
                     }
                 }
-                int4 v[8];
-                if (src) {
-                    #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const int4*>(src) + j);
-                } else {
-                    #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] = make_int4(0, 0, 0, 0);
+                if (!mbar_wait(&empty[s], ph ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
+                if (!staged) {
+                    const int k = (kb0 + i) * Cfg::BK + half * 32;
+                    const int32_t* src = nullptr;
+                    if (live && k < a.K) {
+                        if (SRC == SRC_X32) src = a.x + size_t(grow) * a.ldx + k;
+                        else {
+                            const int tap = k / a.C, c0 = k - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
+                            const int iy = iy0 + ky, ix = ix0 + kx;
+                            if (iy >= 0 && iy < a.H && ix >= 0 && ix < a.W) src = a.img + ((size_t(cb) * a.H + iy) * a.W + ix) * a.C + c0;
+                        }
+                    }
+                    if (src) {
+                        #pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const int4*>(src) + j);
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = make_int4(0, 0, 0, 0);
+                    }
                 }
                 uint32_t hw[8], lw[8];
                 #pragma unroll
@@ -325,14 +379,16 @@ template <int BN, int STAGES, int SRC, int EPI>
 void launch_gemm(const GemmArgs& a, int splits, cudaStream_t st) {
     using Cfg = GemmCfg<BN, STAGES>;
     auto kern = gemm_w8a16_kernel<BN, STAGES, SRC, EPI>;
+    constexpr int SMEM_MAX = (SRC != SRC_I8 && Cfg::X_STAGES > 0) ? Cfg::SMEM_X : Cfg::SMEM;
     static int attr_done[64] = {0};
     const int dev = current_device();
     if (dev >= 64 || !attr_done[dev]) {
-        VELA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        VELA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         if (dev < 64) attr_done[dev] = 1;
     }
+    VELA_REQUIRE(!a.xtma || (SRC != SRC_I8 && Cfg::X_STAGES > 0), "gemm: TMA-staged int32 operand without a staging ring");
     dim3 grid(ceil_div(a.Np, BN), ceil_div(a.Mp, 128), splits);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a);
+    kern<<<grid, Cfg::THREADS, a.xtma ? Cfg::SMEM_X : Cfg::SMEM, st>>>(a);
     VELA_CUDA(cudaGetLastError());
 }
 
