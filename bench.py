@@ -64,8 +64,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention"], default=None,
-                    help="run only the named kernel at its bench shape (for profiler captures) and exit")
+    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv"], default=None,
+                    help="run only the named kernel(s) at the BASELINE config shape (attention: config 2, gemm: config 1, "
+                         "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 for 640 ch 32x32 / 1280 ch 16x16), "
+                         "print their CUDA-event times as one JSON line and exit")
+    ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2])
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -232,6 +235,125 @@ class AttentionCase:
         e1.synchronize()
         assert self.L.vela_device_error(1) == 0, "attention kernel reported a device error"
         return e0.elapsed_time(e1) / iters
+
+
+def _time_ms(stream, fn, warmup=3, iters=10):
+    import torch
+    for _ in range(warmup):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(iters):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+class GemmCase:
+    """Config 1: planar A (hi/lo of int16 uniform over [-32768, 32767]) M 4096 x K 320, W int8 320 x 320, e in [0, 12)."""
+
+    def __init__(self, device):
+        import ctypes
+        import torch
+        import vela_b200 as V
+        from vela_b200 import abi
+        self.t, self.V, self.L = torch, V, V.lib()
+        M, N, K = 4096, 320, 320
+        g = torch.Generator(device=device); g.manual_seed(1)
+        q = torch.randint(-32768, 32768, (M, K), generator=g, device=device, dtype=torch.int32)
+        self.hi = (q >> 8).to(torch.int8); self.lo = ((q & 255) - 128).to(torch.int8)
+        self.W = torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int32).to(torch.int8)
+        cst = torch.zeros((N, 4), dtype=torch.int32, device=device)
+        cst[:, 0] = torch.randint(16384, 32768, (N,), generator=g, device=device, dtype=torch.int32)
+        cst[:, 1] = torch.randint(20, 30, (N,), generator=g, device=device, dtype=torch.int32)
+        cst[:, 2] = torch.randint(-50000, 50000, (N,), generator=g, device=device, dtype=torch.int32)
+        cst[:, 3] = self.W.to(torch.int32).sum(1)
+        self.cst = cst
+        self.e = torch.randint(0, 12, (M,), generator=g, device=device, dtype=torch.int32)
+        self.Y = torch.empty((M, N), dtype=torch.int32, device=device)
+        a = abi.ASrc(); a.src = abi.SRC_I8; a.hi = self.hi.data_ptr(); a.lo = self.lo.data_ptr(); a.ld8 = K; a.e = self.e.data_ptr()
+        E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = self.Y.data_ptr(); E.ldy = N
+        self.a, self.E, self.shape = a, E, (M, N, K)
+        self.stream = torch.cuda.current_stream(device)
+        self.ptr = ctypes.c_void_p
+        self.byref = ctypes.byref
+
+    def launch(self):
+        M, N, K = self.shape
+        self.V.check(self.L.vela_gemm_w8a16(self.stream.cuda_stream, self.byref(self.a), M, M, self.ptr(self.W.data_ptr()), K, N, N, K,
+                                            self.ptr(self.cst.data_ptr()), self.byref(self.E)))
+
+    def report(self):
+        M, N, K = self.shape
+        ms = _time_ms(self.stream, self.launch)
+        ops = 2 * 2 * M * N * K
+        byt = M * K * 2 + N * K + M * 4 + M * N * 4
+        return {"kernel": "gemm_w8a16 planar (config 1)", "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                "int8_tops": round(ops / ms / 1e9, 2), "gbs": round(byt / ms / 1e6, 1)}
+
+
+class GnConvCase:
+    """Config 3: GroupNorm (32 groups) + SiLU of int32 NHWC [8, H*W, C] (uniform over the int16 range), pixel max,
+    3x3 window exponents, then the implicit 3x3 conv C -> C with int8 weights."""
+    LEVELS = [(64, 320), (32, 640), (16, 1280)]
+
+    def __init__(self, device, level):
+        import ctypes
+        import torch
+        import vela_b200 as V
+        from vela_b200 import abi
+        self.t, self.V, self.L = torch, V, V.lib()
+        Hh, C = self.LEVELS[level]
+        B, T, N, K = 8, Hh * Hh, C, 9 * C
+        g = torch.Generator(device=device); g.manual_seed(3)
+        ri = lambda lo, hi, shape: torch.randint(lo, hi, shape, generator=g, device=device, dtype=torch.int32)
+        self.X = ri(-32768, 32768, (B, T, C))
+        self.gam = ri(65536 - 16384, 65536 + 16384, (C,)); self.beta = ri(-8192, 8192, (C,))
+        xs = np.arange(2049, dtype=np.float64) / 64.0 - 16.0
+        self.Lsig = torch.from_numpy(np.rint(65536.0 / (1.0 + np.exp(-xs))).astype(np.int32)).to(device)
+        self.gs = torch.zeros((B * 32, 6), dtype=torch.int64, device=device)
+        self.Y = torch.empty((B, T, C), dtype=torch.int32, device=device)
+        self.pm = torch.empty((B * T,), dtype=torch.int32, device=device)
+        self.ce = torch.empty((B * T,), dtype=torch.int32, device=device)
+        self.W = ri(-127, 128, (N, K)).to(torch.int8)
+        cst = torch.zeros((N, 4), dtype=torch.int32, device=device)
+        cst[:, 0] = ri(16384, 32768, (N,)); cst[:, 1] = ri(20, 30, (N,)); cst[:, 2] = ri(-50000, 50000, (N,)); cst[:, 3] = self.W.to(torch.int32).sum(1)
+        self.cst = cst
+        self.out = torch.empty((B, T, N), dtype=torch.int32, device=device)
+        a = abi.ASrc(); a.src = abi.SRC_CONV32; a.img = self.Y.data_ptr(); a.H = Hh; a.W = Hh; a.C = C; a.stride = 1; a.Ho = Hh; a.Wo = Hh
+        a.K = K; a.e = self.ce.data_ptr()
+        E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = self.out.data_ptr(); E.ldy = N
+        self.a, self.E, self.dims = a, E, (B, Hh, C, T, N, K)
+        self.stream = torch.cuda.current_stream(device)
+        self.P = lambda x: ctypes.c_void_p(x.data_ptr())
+        self.byref = ctypes.byref
+
+    def gn(self):
+        B, Hh, C, T, N, K = self.dims
+        st, P = self.stream.cuda_stream, self.P
+        self.V.check(self.L.vela_gn_stats(st, P(self.X), B, T, C, 32, 100000, P(self.gs)))
+        self.V.check(self.L.vela_gn_apply_row(st, P(self.X), B, T, C, 32, P(self.gs), P(self.gam), P(self.beta), P(self.Lsig),
+                                              P(self.Y), P(self.pm), None, None, None, 0))
+
+    def conv(self):
+        B, Hh, C, T, N, K = self.dims
+        st, P = self.stream.cuda_stream, self.P
+        self.V.check(self.L.vela_conv_e(st, P(self.pm), B, Hh, Hh, 1, P(self.ce)))
+        self.V.check(self.L.vela_gemm_w8a16(st, self.byref(self.a), B * T, B * T, P(self.W), K, N, N, K, P(self.cst), self.byref(self.E)))
+
+    def launch(self):
+        self.gn(); self.conv()
+
+    def report(self):
+        B, Hh, C, T, N, K = self.dims
+        self.gn()
+        gms, cms = _time_ms(self.stream, self.gn), _time_ms(self.stream, self.conv)
+        ops = 2 * 2 * B * T * N * K
+        return {"kernel": "GroupNorm+SiLU -> implicit 3x3 conv (config 3)", "B": B, "HW": Hh, "C": C,
+                "gn_ms": round(gms, 4), "gn_gbs": round(B * T * C * 8 / gms / 1e6, 1),
+                "conv_ms": round(cms, 4), "conv_int8_tops": round(ops / cms / 1e9, 2)}
 
 
 # ------------------------------------------------------------------ CPU baseline (the oracle, bounded sample)
@@ -426,11 +548,22 @@ def run_reference(a, R):
 
 def run_kernel(a, R):
     import torch
-    case = AttentionCase(torch.device("cuda", R.local))
-    for _ in range(3):
-        case.launch()
+    dev = torch.device("cuda", R.local)
+    if a.kernel == "attention":
+        case = AttentionCase(dev)
+        for _ in range(3):
+            case.launch()
+        rep = {"kernel": "attention (config 2)", "ms": round(case.time_ms(), 4)}
+    elif a.kernel == "gemm":
+        case = GemmCase(dev)
+        rep = case.report()
+    else:
+        case = GnConvCase(dev, a.conv_level)
+        rep = case.report()
     torch.cuda.synchronize()
-    assert case.L.vela_device_error(1) == 0
+    assert case.L.vela_device_error(1) == 0, "a kernel reported a device error"
+    if R.rank == 0:
+        print(json.dumps(rep), flush=True)
 
 
 def main():

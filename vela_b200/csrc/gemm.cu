@@ -2,9 +2,11 @@
 // Replaces the reference's k_gemm_hl / k_gemm_hl2 (src/gemm_hl.h:27-33) and,
 // for deep K, its cuBLASLt + k_epilogue path (src/engine.cu:153-157).
 #include "gemm_kernel.cuh"
+#include "gemm_persist.cuh"
 #include "host_util.h"
 #include "vela_b200.h"
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -41,31 +43,57 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 }
 
 // the instantiations live in gemm_inst_*.cu
-#define VELA_GEMM_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm<BN, ST, SRC, EPI>(const GemmArgs&, int, cudaStream_t);
-VELA_GEMM_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_PLAIN) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_PLAIN)
-VELA_GEMM_EXTERN(64, 3, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 3, SRC_X32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 3, SRC_X32, EPI_PLAIN)
-VELA_GEMM_EXTERN(64, 3, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(128, 3, SRC_CONV32, EPI_PLAIN) VELA_GEMM_EXTERN(256, 3, SRC_CONV32, EPI_PLAIN)
-VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_GEGLU) VELA_GEMM_EXTERN(256, 4, SRC_I8, EPI_GEGLU)
-VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_SPLIT3) VELA_GEMM_EXTERN(128, 4, SRC_I8, EPI_QKV)
+#define VELA_PERSIST_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm_persist<BN, ST, SRC, EPI>(const GemmArgs&, cudaStream_t);
+VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
+VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_SPLIT3) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_QKV)
+#define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 3, SRC, EPI_PLAIN) \
+    VELA_PERSIST_EXTERN(160, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(224, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 3, SRC, EPI_PLAIN)
+VELA_PERSIST_REG(SRC_X32) VELA_PERSIST_REG(SRC_CONV32)
 
 namespace {
-// int32 sources run a 3-stage MMA ring: the TMA staging ring of the raw operand holds the prefetch depth
-template <int SRC> void dispatch_plain(int BN, const GemmArgs& a, int splits, cudaStream_t st) {
-    constexpr int S64 = SRC == SRC_I8 ? 6 : 3, S = SRC == SRC_I8 ? 4 : 3;
-    if (BN == 64) launch_gemm<64, S64, SRC, EPI_PLAIN>(a, splits, st);
-    else if (BN == 128) launch_gemm<128, S, SRC, EPI_PLAIN>(a, splits, st);
-    else launch_gemm<256, S, SRC, EPI_PLAIN>(a, splits, st);
+constexpr int REG_BNS[5] = {64, 128, 160, 224, 256};
+
+template <int SRC> void dispatch_reg(int BN, const GemmArgs& a, cudaStream_t st) {
+    switch (BN) {
+        case 64: launch_gemm_persist<64, 3, SRC, EPI_PLAIN>(a, st); break;
+        case 128: launch_gemm_persist<128, 3, SRC, EPI_PLAIN>(a, st); break;
+        case 160: launch_gemm_persist<160, 3, SRC, EPI_PLAIN>(a, st); break;
+        case 224: launch_gemm_persist<224, 3, SRC, EPI_PLAIN>(a, st); break;
+        default: launch_gemm_persist<256, 3, SRC, EPI_PLAIN>(a, st); break;
+    }
+}
+
+struct Plan { int bn, splits; };
+
+// Tile width and K splits from a cost model of the persistent kernel, in units of one 128 x 64 x 64 MMA k-block:
+// a work unit (tile, K range) costs its k-blocks x (operand cost + BN / 64); int32 sources pay the quantising of the
+// 128 x 64 A block again for every column tile (measured ~10 units), planar sources only the TMA (~0.5).  The units
+// are spread over the SMs in waves; a K split adds the partial-sum traffic of its reduction.
+Plan plan(int src, int epi, int Mp, int Mreal, int Np, int Nreal, int nkb, size_t workspace, int sms) {
+    if (epi != EPI_PLAIN) return {128, 1};
+    const bool reg = src != VELA_SRC_I8;
+    const double per_kb = reg ? 10.0 : 0.5, us_per_unit = 0.065;
+    const int nM = ceil_div(Mp, 128);
+    Plan best{reg ? 128 : 64, 1};
+    double best_t = 1e30;
+    const int nb = reg ? 5 : 2;
+    const int i8_bns[2] = {64, 128};
+    for (int i = 0; i < nb; ++i) {
+        const int bn = reg ? REG_BNS[i] : i8_bns[i];
+        if (!reg && bn == 128 && Nreal % 128 != 0 && Nreal > 128) continue;
+        const int nN = ceil_div(Np, bn);
+        for (int s = 1; s <= 8; ++s) {
+            if (s > 1 && (size_t(s) * 2 * Mp * Np * 4 > workspace || ceil_div(nkb, s) < 4)) break;
+            const int kbs = ceil_div(nkb, s), units = nN * nM * s;
+            const double waves = double(ceil_div(units, sms));
+            double t = waves * kbs * (per_kb + bn / 64.0) * us_per_unit;
+            if (s > 1) t += (double(s) * 8 + 8) * Mreal * Nreal / 6.0e6 + 3.0;     // partials in and out of HBM + a launch
+            if (t < best_t * 0.98) { best_t = t; best = {bn, s}; }
+        }
+    }
+    return best;
 }
 }  // namespace
-
-// Tile width: the fewest column tiles, then the least padding.
-static int pick_bn(int Nreal, int epi) {
-    if (epi == EPI_QKV || epi == EPI_SPLIT3) return 128;
-    if (epi == EPI_GEGLU) return (Nreal % 256 == 0) ? 256 : 128;
-    if (Nreal % 256 == 0 && Nreal >= 1024) return 256;
-    if (Nreal % 128 == 0) return 128;
-    return 64;
-}
 
 void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
                 const int32_t* cst, const vela_aepi& E) {
@@ -132,32 +160,22 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
         throw Error(VELA_ERR_ARG, "gemm: unknown A source");
     }
     if (epi != EPI_PLAIN) VELA_REQUIRE(src == VELA_SRC_I8, "gemm: GEGLU / split3 / q|k|v epilogues take planar int8 operands");
-    const int BN = pick_bn(Nreal, epi);
-    a.tmW = tmap2d(W, CU_TENSOR_MAP_DATA_TYPE_UINT8, uint64_t(Kp), uint64_t(Np), uint64_t(ldw), 64, uint32_t(BN), Swz::B64);
 
-    // split-K when the output tiles cannot fill the GPU and K is deep (exact: integer partial sums)
-    int splits = 1;
-    const int tiles = ceil_div(Np, BN) * ceil_div(Mp, 128), sms = sm_count();
-    if (epi == EPI_PLAIN && E.workspace && tiles * 2 <= sms && a.nkb >= 16) {
-        splits = std::min({sms / tiles, a.nkb / 8, 16});
-        const size_t need = size_t(splits) * 2 * Mp * Np * 4;
-        if (splits < 2 || need > E.workspace_bytes || Nreal % 4 != 0 || E.ldy % 4 != 0) splits = 1;
-    }
-    a.kb_per_split = ceil_div(a.nkb, splits);
-    splits = ceil_div(a.nkb, a.kb_per_split);
+    const bool splittable = epi == EPI_PLAIN && E.workspace && Nreal % 4 == 0 && E.ldy % 4 == 0;
+    const Plan pl = plan(src, epi, Mp, Mreal, Np, Nreal, a.nkb, splittable ? E.workspace_bytes : 0, sm_count());
+    const int BN = pl.bn;
+    a.tmW = tmap2d(W, CU_TENSOR_MAP_DATA_TYPE_UINT8, uint64_t(Kp), uint64_t(Np), uint64_t(ldw), 64, uint32_t(BN), Swz::B64);
+    a.kb_per_split = ceil_div(a.nkb, pl.splits);
+    const int splits = ceil_div(a.nkb, a.kb_per_split);
     if (splits > 1) a.partial = static_cast<int32_t*>(E.workspace);
 
     if (epi == EPI_PLAIN) {
-        if (src == VELA_SRC_I8) dispatch_plain<SRC_I8>(BN, a, splits, st);
-        else if (src == VELA_SRC_X32) dispatch_plain<SRC_X32>(BN, a, splits, st);
-        else dispatch_plain<SRC_CONV32>(BN, a, splits, st);
-    } else if (epi == EPI_GEGLU) {
-        if (BN == 256) launch_gemm<256, 4, SRC_I8, EPI_GEGLU>(a, 1, st); else launch_gemm<128, 4, SRC_I8, EPI_GEGLU>(a, 1, st);
-    } else if (epi == EPI_SPLIT3) {
-        launch_gemm<128, 4, SRC_I8, EPI_SPLIT3>(a, 1, st);
-    } else {
-        launch_gemm<128, 4, SRC_I8, EPI_QKV>(a, 1, st);
-    }
+        if (src == VELA_SRC_I8) { if (BN == 128) launch_gemm_persist<128, 6, SRC_I8, EPI_PLAIN>(a, st); else launch_gemm_persist<64, 6, SRC_I8, EPI_PLAIN>(a, st); }
+        else if (src == VELA_SRC_X32) dispatch_reg<SRC_X32>(BN, a, st);
+        else dispatch_reg<SRC_CONV32>(BN, a, st);
+    } else if (epi == EPI_GEGLU) launch_gemm_persist<128, 6, SRC_I8, EPI_GEGLU>(a, st);
+    else if (epi == EPI_SPLIT3) launch_gemm_persist<128, 6, SRC_I8, EPI_SPLIT3>(a, st);
+    else launch_gemm_persist<128, 6, SRC_I8, EPI_QKV>(a, st);
     if (splits > 1) {
         const size_t n = size_t(Mreal) * (Nreal / 4);
         gemm_splitk_reduce<<<unsigned((n + 255) / 256), 256, 0, st>>>(a.partial, splits, Mp, Np, Mreal, Nreal, a.cst, a.e, a.rowmax_in, src == VELA_SRC_X32,

@@ -1,7 +1,9 @@
-// Explicit instantiations of the W8A16 GEMM (split across files to compile in parallel).
-#include "gemm_kernel.cuh"
+// Explicit instantiations of the persistent W8A16 GEMM (split across files to compile in parallel): planar sources.
+#include "gemm_persist.cuh"
 namespace vela {
-template void launch_gemm<64, 6, SRC_I8, EPI_PLAIN>(const GemmArgs&, int, cudaStream_t);
-template void launch_gemm<128, 4, SRC_I8, EPI_PLAIN>(const GemmArgs&, int, cudaStream_t);
-template void launch_gemm<256, 4, SRC_I8, EPI_PLAIN>(const GemmArgs&, int, cudaStream_t);
+template void launch_gemm_persist<64, 6, SRC_I8, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
+template void launch_gemm_persist<128, 6, SRC_I8, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
+template void launch_gemm_persist<128, 6, SRC_I8, EPI_GEGLU>(const GemmArgs&, cudaStream_t);
+template void launch_gemm_persist<128, 6, SRC_I8, EPI_SPLIT3>(const GemmArgs&, cudaStream_t);
+template void launch_gemm_persist<128, 6, SRC_I8, EPI_QKV>(const GemmArgs&, cudaStream_t);
 }  // namespace vela

@@ -1,0 +1,261 @@
+// Persistent W8A16 GEMM on the sm_100a tensor cores: one CTA per SM walks the output tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... (column tiles fastest, so the CTAs in flight share A rows in L2).
+//
+// Same arithmetic, operand sources and epilogues as gemm_w8a16_kernel (gemm_kernel.cuh); what changes is the
+// schedule.  Two TMEM accumulator buffers (2 x [hi | lo] x BN columns) let the epilogue of tile i run while the
+// MMAs of tile i+1 accumulate, and the TMA / converter rings run continuously across tile boundaries, so the
+// short-K GEMMs of the UNet (K = 320..1280, 5-20 k-blocks per tile) no longer pay a pipeline fill, a TMEM
+// allocation and an exposed epilogue per tile.
+//
+// Warp roles (THREADS = 32 x (2 + NCW + 8)):
+//   warp 0            TMA producer: W (and A-hi / A-lo planes, or the raw int32 operand into the staging ring)
+//   warp 1            TMEM allocator and MMA issuer (one elected lane)
+//   warps 2 .. 1+NCW  int32 sources only (NCW = 8): quantise the staged rows into the swizzled A tiles
+//   last 8 warps      epilogue: warp % 4 selects the TMEM lane quarter, the two warps of a quarter split the columns
+// Every wait is bounded; on a timeout the error word is set and each role stops issuing work.
+#pragma once
+#include "gemm_kernel.cuh"
+#include <algorithm>
+
+namespace vela {
+
+template <int BN, int STAGES, int SRC> struct PersistCfg {
+    static constexpr bool REG = SRC != SRC_I8;
+    static constexpr int BM = 128, BK = 64;
+    static constexpr int A_BYTES = BM * BK, W_BYTES = BN * BK;
+    static constexpr int STAGE = 2 * A_BYTES + W_BYTES;
+    static constexpr int ACC_COLS = 2 * BN;                     // hi | lo of one tile
+    static constexpr int ACC_BUFS = 4 * BN <= 512 ? 2 : 1;      // wide tiles (BN > 128) keep one accumulator
+    static constexpr int TCOLS = ACC_BUFS * ACC_COLS;
+    static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : (TCOLS <= 64 ? 64 : (TCOLS <= 128 ? 128 : (TCOLS <= 256 ? 256 : 512)));
+    static constexpr int NCW = REG ? 8 : 0;
+    static constexpr int EPI_WARP0 = 2 + NCW;
+    static constexpr int THREADS = 32 * (2 + NCW + 8);
+    static constexpr int CTRL = 1024;
+    static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
+    static constexpr int OFF_X = (STAGES * STAGE + CTRL + 1023) / 1024 * 1024;
+    static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
+    static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
+    static constexpr int SMEM = 1024 + OFF_X + (X_STAGES > 0 ? X_STAGES : 0) * X_STAGE;
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "MMA N");
+    static_assert(STAGE % 1024 == 0, "stage alignment");
+    static_assert(!REG || X_STAGES >= 2, "int32 sources need a staging ring of at least two stages");
+};
+
+template <int BN, int STAGES, int SRC, int EPI>
+__global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_persist_kernel(const __grid_constant__ GemmArgs a) {
+    using Cfg = PersistCfg<BN, STAGES, SRC>;
+    constexpr bool REG = Cfg::REG;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accf = empty + STAGES;            // [2] accumulator buffer b holds a finished tile
+    uint64_t* acce = accf + 2;                  // [2] the epilogue has drained buffer b
+    uint64_t* xfull = acce + 2;                 // [4] int32 staging ring
+    uint64_t* xempty = xfull + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 4);
+    uint8_t* xstage = smem + Cfg::OFF_X;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nN = (a.Np + BN - 1) / BN, nM = (a.Mp + Cfg::BM - 1) / Cfg::BM;
+    // work unit t = (K split z, row tile, column tile), column tiles fastest; split-K writes raw partials
+    const int nMN = nN * nM, kbs = a.kb_per_split, nsplit = (a.nkb + kbs - 1) / kbs;
+    const int ntiles = nMN * nsplit;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1 + Cfg::NCW); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 8); }
+        for (int s = 0; s < 4; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], Cfg::NCW > 0 ? Cfg::NCW : 1); }
+        mbar_fence_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&a.tmW);
+        if (SRC == SRC_I8) { tma_prefetch_desc(&a.tmA_hi); tma_prefetch_desc(&a.tmA_lo); }
+        if (REG && a.xtma) tma_prefetch_desc(&a.tmX);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM, n0 = (r % nN) * BN;
+                const int kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
+                int cb = 0, cy0 = 0;
+                if (SRC == SRC_CONV32 && a.xtma) { cb = m0 / a.conv_rows_per_img; cy0 = (m0 - cb * a.conv_rows_per_img) / a.Wo; }
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int k = (kb0 + i) * Cfg::BK;
+                    if constexpr (REG) {
+                        if (a.xtma) {
+                            const int xs = g % Cfg::X_STAGES;
+                            if (!mbar_wait(&xempty[xs], ((g / Cfg::X_STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                            mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
+                            #pragma unroll
+                            for (int hf = 0; hf < 2; ++hf) {
+                                uint8_t* dst = xstage + xs * Cfg::X_STAGE + hf * Cfg::X_HALF;
+                                const int kk = k + hf * 32;
+                                if (SRC == SRC_X32) tma_load_2d(dst, &a.tmX, &xfull[xs], kk, m0);
+                                else {
+                                    const int tap = kk / a.C, c0 = kk - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
+                                    const int yy = tap < 9 ? cy0 * a.stride + ky - 1 : a.H + 8;   // K padding: a box below the image
+                                    tma_load_4d(dst, &a.tmX, &xfull[xs], tap < 9 ? c0 : 0, kx - 1, yy, cb);
+                                }
+                            }
+                        }
+                    }
+                    const int s = g % STAGES;
+                    if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    uint8_t* st = smem + s * Cfg::STAGE;
+                    mbar_arrive_expect_tx(&full[s], Cfg::W_BYTES + (SRC == SRC_I8 ? 2 * Cfg::A_BYTES : 0));
+                    tma_load_2d(st + 2 * Cfg::A_BYTES, &a.tmW, &full[s], k, n0);
+                    if (SRC == SRC_I8) {
+                        tma_load_2d(st, &a.tmA_hi, &full[s], k, m0);
+                        tma_load_2d(st + Cfg::A_BYTES, &a.tmA_lo, &full[s], k, m0);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(128, BN);
+            int g = 0, tl = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tl) {
+                const int b = Cfg::ACC_BUFS == 2 ? (tl & 1) : 0, u = Cfg::ACC_BUFS == 2 ? (tl >> 1) : tl;
+                if (!mbar_wait(&acce[b], (u & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(b * Cfg::ACC_COLS);
+                const int z = t / nMN, kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(&full[s], (g / STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * Cfg::STAGE);
+                    #pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const uint64_t bd = sdesc_sw64(sa + 2 * Cfg::A_BYTES + kk * 32);
+                        mma_i8(d, sdesc_sw64(sa + kk * 32), bd, idesc, (i | kk) != 0);
+                        mma_i8(d + BN, sdesc_sw64(sa + Cfg::A_BYTES + kk * 32), bd, idesc, (i | kk) != 0);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&accf[b]);     // fires when every MMA of this tile has completed
+            }
+        }
+    } else if (REG && warp < Cfg::EPI_WARP0) {
+        // ------------------------------------------------------------ A producers (int32 sources)
+        const int ct = threadIdx.x - 64;                  // 0..255: row = ct & 127, K half = ct >> 7
+        const int row = ct & 127, half = ct >> 7;
+        int g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const int z = t / nMN, m0 = ((t - z * nMN) / nN) * Cfg::BM;
+            const int kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
+            const int grow = m0 + row;
+            const bool live = grow < a.Mreal;
+            int er = 0, cb = 0, iy0 = 0, ix0 = 0;
+            if (SRC == SRC_X32) er = live ? row_exp(a.rowmax_in[grow]) : 0;
+            else {
+                er = live ? a.e[grow] : 0;
+                const int hw = a.Ho * a.Wo; cb = grow / hw; const int p = grow - cb * hw; const int oy = p / a.Wo, ox = p - oy * a.Wo;
+                iy0 = oy * a.stride - 1; ix0 = ox * a.stride - 1;
+            }
+            // quant16(v, e) = clamp(((v >> (e-1)) + 1) >> 1) for e >= 1, clamp(v) for e = 0
+            const int qs1 = er > 0 ? er - 1 : 0, qr = er > 0 ? 1 : 0, qs2 = er > 0 ? 1 : 0;
+            for (int i = 0; i < nk; ++i, ++g) {
+                int4 v[8];
+                if (a.xtma) {
+                    const int xs = g % Cfg::X_STAGES;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::X_STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL))) { ok = false; break; }
+                    const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
+                    #pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xempty[xs]);
+                } else {
+                    const int k = (kb0 + i) * Cfg::BK + half * 32;
+                    const int32_t* src = nullptr;
+                    if (live && k < a.K) {
+                        if (SRC == SRC_X32) src = a.x + size_t(grow) * a.ldx + k;
+                        else {
+                            const int tap = k / a.C, c0 = k - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
+                            const int iy = iy0 + ky, ix = ix0 + kx;
+                            if (iy >= 0 && iy < a.H && ix >= 0 && ix < a.W) src = a.img + ((size_t(cb) * a.H + iy) * a.W + ix) * a.C + c0;
+                        }
+                    }
+                    if (src) {
+                        #pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const int4*>(src) + j);
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = make_int4(0, 0, 0, 0);
+                    }
+                }
+                const int s = g % STAGES;
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY))) { ok = false; break; }
+                uint32_t hw[8], lw[8];
+                #pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int q0 = quant16_fast(v[j].x, qs1, qr, qs2), q1 = quant16_fast(v[j].y, qs1, qr, qs2);
+                    const int q2 = quant16_fast(v[j].z, qs1, qr, qs2), q3 = quant16_fast(v[j].w, qs1, qr, qs2);
+                    hw[j] = pack_hi4(q0, q1, q2, q3); lw[j] = pack_lo4(q0, q1, q2, q3);
+                }
+                uint8_t* st = smem + s * Cfg::STAGE;
+                *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2 + 1)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                *reinterpret_cast<uint4*>(st + Cfg::A_BYTES + sw64_off(row, half * 2)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                *reinterpret_cast<uint4*>(st + Cfg::A_BYTES + sw64_off(row, half * 2 + 1)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - Cfg::EPI_WARP0;            // 0..7
+        const int q = warp & 3, h = ew >> 2;             // TMEM lane quarter (fixed by warp % 4), column half
+        const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
+        int tl = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+            const int b = Cfg::ACC_BUFS == 2 ? (tl & 1) : 0, u = Cfg::ACC_BUFS == 2 ? (tl >> 1) : tl;
+            if (!__all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC))) break;
+            tc_fence_after();
+            const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM, n0 = (r % nN) * BN;
+            gemm_epilogue<BN, SRC, EPI>(a, tq + uint32_t(b * Cfg::ACC_COLS), a.cst + n0, m0, n0, q * 32 + lane, h, z);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) { tc_fence_after(); tmem_dealloc(tmem, Cfg::TMEM_COLS); }
+}
+
+template <int BN, int STAGES, int SRC, int EPI>
+void launch_gemm_persist(const GemmArgs& a, cudaStream_t st) {
+    using Cfg = PersistCfg<BN, STAGES, SRC>;
+    auto kern = gemm_persist_kernel<BN, STAGES, SRC, EPI>;
+    static int attr_done[64] = {0};
+    const int dev = current_device();
+    if (dev >= 64 || !attr_done[dev]) {
+        VELA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        if (dev < 64) attr_done[dev] = 1;
+    }
+    VELA_REQUIRE(a.kb_per_split > 0 && (a.partial != nullptr) == (a.kb_per_split < a.nkb) && (EPI == EPI_PLAIN || a.partial == nullptr),
+                 "gemm: split-K needs a workspace and the plain epilogue");
+    const int tiles = ceil_div(a.Np, BN) * ceil_div(a.Mp, 128) * ceil_div(a.nkb, a.kb_per_split);
+    const int grid = std::min(tiles, sm_count());
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a);
+    VELA_CUDA(cudaGetLastError());
+}
+
+}  // namespace vela

@@ -50,6 +50,11 @@ __device__ __forceinline__ int quant16(int v, int e) {
     const int q = e ? (v >> e) + ((v >> (e - 1)) & 1) : v;
     return min(max(q, -32767), 32767);
 }
+// quant16 with the row's shift split as (s1, r, s2) = (e - 1, 1, 1) for e >= 1 and (0, 0, 0) for e = 0:
+// ((v >> s1) + r) >> s2 = floor((v + 2^(e-1)) / 2^e) without overflow, then the +-32767 clamp.
+__device__ __forceinline__ int quant16_fast(int v, int s1, int r, int s2) {
+    return min(max(((v >> s1) + r) >> s2, -32767), 32767);
+}
 // hi bytes / lo bytes of four 16-bit values packed into one word each
 __device__ __forceinline__ u32 pack_hi4(int q0, int q1, int q2, int q3) {
     return __byte_perm(__byte_perm(q0, q1, 0x0051), __byte_perm(q2, q3, 0x0051), 0x5410);
