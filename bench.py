@@ -64,10 +64,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu"], default=None,
                     help="run only the named kernel(s) at the BASELINE config shape (attention: config 2, gemm: config 1, "
                          "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 for 640 ch 32x32 / 1280 ch 16x16), "
+                         "linear: the UNet's int32-input linear with residual at 64x64 (M 32768, K --linear-k, N 320), "
+                         "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); "
                          "print their CUDA-event times as one JSON line and exit")
+    ap.add_argument("--linear-k", type=int, default=320)
     ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2])
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
@@ -356,6 +359,60 @@ class GnConvCase:
                 "conv_ms": round(cms, 4), "conv_int8_tops": round(ops / cms / 1e9, 2)}
 
 
+class LinearCase:
+    """The UNet's linears at the 64x64 level: int32 activations [32768, K] quantised on load (row max given),
+    N 320, plain epilogue with residual and row max (proj_out / to_out: K 320; ff.net.2: K 1280); or the GEGLU
+    GEMM on LayerNorm planes (K 320, N 2 x 1280 interleaved a|g)."""
+
+    def __init__(self, device, kind, K):
+        import ctypes
+        import torch
+        import vela_b200 as V
+        from vela_b200 import abi
+        self.t, self.V, self.L = torch, V, V.lib()
+        M = 32768
+        N = 2560 if kind == "geglu" else 320
+        g = torch.Generator(device=device); g.manual_seed(4)
+        ri = lambda lo, hi, shape: torch.randint(lo, hi, shape, generator=g, device=device, dtype=torch.int32)
+        self.W = ri(-127, 128, (N, K)).to(torch.int8)
+        cst = torch.zeros((N, 4), dtype=torch.int32, device=device)
+        cst[:, 0] = ri(16384, 32768, (N,)); cst[:, 1] = ri(20, 30, (N,)); cst[:, 2] = ri(-50000, 50000, (N,)); cst[:, 3] = self.W.to(torch.int32).sum(1)
+        self.cst = cst
+        self.rm_out = torch.zeros((M,), dtype=torch.int32, device=device)
+        a = abi.ASrc(); E = abi.AEpi()
+        if kind == "geglu":
+            q = ri(-32768, 32768, (M, K))
+            self.hi = (q >> 8).to(torch.int8); self.lo = ((q & 255) - 128).to(torch.int8); self.e = ri(0, 6, (M,))
+            a.src = abi.SRC_I8; a.hi = self.hi.data_ptr(); a.lo = self.lo.data_ptr(); a.ld8 = K; a.e = self.e.data_ptr()
+            xs = np.arange(2049, dtype=np.float64) / 64.0 - 16.0
+            from math import erf, sqrt
+            self.Lphi = torch.from_numpy(np.rint([65536.0 * 0.5 * (1 + erf(x / sqrt(2))) for x in xs]).astype(np.int32)).to(device)
+            self.Y = torch.empty((M, N // 2), dtype=torch.int32, device=device)
+            E.epi = abi.EPI_GEGLU; E.Y = self.Y.data_ptr(); E.ldy = N // 2; E.Lphi = self.Lphi.data_ptr(); E.rowmax = self.rm_out.data_ptr()
+        else:
+            self.X = ri(-(1 << 20), 1 << 20, (M, K))
+            self.rm_in = self.X.abs().amax(1).to(torch.int32)
+            self.R = ri(-(1 << 20), 1 << 20, (M, N))
+            self.Y = torch.empty((M, N), dtype=torch.int32, device=device)
+            a.src = abi.SRC_X32; a.x = self.X.data_ptr(); a.ldx = K; a.K = K; a.rowmax = self.rm_in.data_ptr()
+            E.epi = abi.EPI_PLAIN; E.Y = self.Y.data_ptr(); E.ldy = N; E.residual = self.R.data_ptr(); E.rowmax = self.rm_out.data_ptr()
+        self.a, self.E, self.shape, self.kind = a, E, (M, N, K), kind
+        self.stream = torch.cuda.current_stream(device)
+        self.ptr = ctypes.c_void_p
+        self.byref = ctypes.byref
+
+    def launch(self):
+        M, N, K = self.shape
+        self.V.check(self.L.vela_gemm_w8a16(self.stream.cuda_stream, self.byref(self.a), M, M, self.ptr(self.W.data_ptr()), K, N, N, K,
+                                            self.ptr(self.cst.data_ptr()), self.byref(self.E)))
+
+    def report(self):
+        M, N, K = self.shape
+        ms = _time_ms(self.stream, self.launch)
+        return {"kernel": f"gemm_w8a16 {self.kind} (64x64 level)", "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
+
+
 # ------------------------------------------------------------------ CPU baseline (the oracle, bounded sample)
 def cpu_baseline(path):
     from oracle import pyoracle as O
@@ -556,6 +613,9 @@ def run_kernel(a, R):
         rep = {"kernel": "attention (config 2)", "ms": round(case.time_ms(), 4)}
     elif a.kernel == "gemm":
         case = GemmCase(dev)
+        rep = case.report()
+    elif a.kernel in ("linear", "geglu"):
+        case = LinearCase(dev, a.kernel, a.linear_k if a.kernel == "linear" else 320)
         rep = case.report()
     else:
         case = GnConvCase(dev, a.conv_level)

@@ -107,6 +107,7 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
     a.nkb = ceil_div(Kp, 64);
     a.cst = reinterpret_cast<const int4*>(cst);
     a.Y = E.Y; a.ldy = E.ldy; a.R = E.residual; a.Lphi = E.Lphi; a.rowmax_out = E.rowmax;
+    a.rvec = E.residual && (E.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(E.residual) & 15) == 0;
     a.gelu = E.epi == VELA_EPI_GELU;
     a.Cs = E.Cs; a.Y1 = E.Y1; a.Y2 = E.Y2;
     a.heads = E.heads; a.T = E.T; a.TpQ = E.TpQ; a.TpK = E.TpK; a.Cq = E.C;

@@ -37,32 +37,43 @@ struct GemmArgs {
     int heads, T, TpQ, TpK, Cq;                             // EPI_QKV (Cq = heads * 64)
     int8_t *qhi, *qlo, *khi, *klo; int32_t *qe, *ke; int64_t *qhs, *qls, *qts, *khs, *kls, *kts;
     int32_t* partial;                                       // split-K: raw s32 [split][2][Mp][Np]
+    int rvec;                                               // residual rows 16-byte aligned (int4 loads)
     unsigned* err;
 };
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }
 
-// Epilogue of one 128 x BN tile for one thread = one output row (rl) and one column half (h, of BN / 2 columns;
-// q|k|v: one 64-column head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
-// applies the per-column constants `cst` (cst[0] = column n0) and writes the epilogue's outputs.
-template <int BN, int SRC, int EPI>
-__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, int m0, int n0, int rl, int h, int split) {
+// lut16 / lut_act (intops.cuh) from a table staged in shared memory as (L[i], L[i+1] - L[i]), i < 2048
+__device__ __forceinline__ int lut16_s(int x, const int2* __restrict__ L2) {
+    if (x < -(16 << 16)) return 0;
+    if (x >= (16 << 16)) return 65536;
+    const int z = x + (16 << 16);
+    const int2 e = L2[z >> 10];
+    return e.x + ((e.y * (z & 1023)) >> 10);
+}
+__device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ L2) { return int(rshr_pos(i64(x) * lut16_s(x, L2), 16)); }
+
+// Epilogue of one 128 x BN tile for one thread = one output row (rl) and the NC columns [c0, c0 + NC) of the tile
+// (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
+// applies the per-column constants (cst[j] = column n0 + j) and writes the epilogue's outputs.  er is the row's
+// exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory).
+template <int BN, int SRC, int EPI, int NC>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
+                                              int m0, int n0, int rl, int c0, int split, int er) {
+    static_assert(NC % 16 == 0, "16-column chunks");
     const int grow = m0 + rl;
     const bool live = grow < a.Mreal;
-    int er = 0;
-    if (live) er = (SRC == SRC_X32) ? row_exp(a.rowmax_in[grow]) : a.e[grow];
-    constexpr int HALF = BN / 2;
     if constexpr (EPI == EPI_QKV) {
-        static_assert(BN == 128, "q|k|v epilogue works on one 64-column head per thread");
+        static_assert(NC == 64, "q|k|v epilogue works on one 64-column head per thread");
         int y[64];
         #pragma unroll
         for (int c = 0; c < 4; ++c) {
             int hi[16], lo[16];
-            tmem_ld16(tl + h * 64 + c * 16, hi); tmem_ld16(tl + BN + h * 64 + c * 16, lo); tmem_ld_wait();
+            tmem_ld16(tl + c0 + c * 16, hi); tmem_ld16(tl + BN + c0 + c * 16, lo); tmem_ld_wait();
             #pragma unroll
-            for (int j = 0; j < 16; ++j) { const int4 cc = cst[h * 64 + c * 16 + j]; y[c * 16 + j] = epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
+            for (int j = 0; j < 16; ++j) { const int4 cc = cst[c0 + c * 16 + j]; y[c * 16 + j] = epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
         }
-        const int nh = n0 + h * 64;
+        const int nh = n0 + c0;
         if (live && nh < a.Nreal) {
             const int part = nh / a.Cq, head = (nh - part * a.Cq) >> 6;
             if (part == 2) {
@@ -103,11 +114,22 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
     } else {
         u32 mx = 0;
         #pragma unroll 1
-        for (int c = 0; c < HALF / 16; ++c) {
-            const int col = h * HALF + c * 16, n = n0 + col;
+        for (int c = 0; c < NC / 16; ++c) {
+            const int col = c0 + c * 16, n = n0 + col;
+            const bool act = live && n < a.Nreal;
+            const bool full16 = n + 16 <= a.Nreal;
+            // residual of this chunk in flight while the accumulators are read (int4 when rows are 16-byte aligned)
+            int4 rv[4];
+            if constexpr (EPI == EPI_PLAIN) {
+                if (act && a.R && a.rvec && full16) {
+                    const int4* rp = reinterpret_cast<const int4*>(a.R + size_t(grow) * a.ldy + n);
+                    #pragma unroll
+                    for (int j = 0; j < 4; ++j) rv[j] = __ldg(rp + j);
+                }
+            }
             int hi[16], lo[16];
             tmem_ld16(tl + col, hi); tmem_ld16(tl + BN + col, lo); tmem_ld_wait();
-            if (!live || n >= a.Nreal) continue;
+            if (!act) continue;
             if (a.partial) {             // split-K: raw accumulators, reduced by gemm_splitk_reduce
                 int32_t* ph = a.partial + (size_t(split) * 2 * a.Mp + grow) * a.Np + n;
                 int32_t* pl = ph + size_t(a.Mp) * a.Np;
@@ -122,15 +144,26 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
             #pragma unroll
             for (int j = 0; j < 16; ++j) { const int4 cc = cst[col + j]; y[j] = epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
             if constexpr (EPI == EPI_PLAIN) {
-                const bool full16 = n + 16 <= a.Nreal;
                 if (a.gelu) {
-                    #pragma unroll
-                    for (int j = 0; j < 16; ++j) y[j] = lut_act(y[j], a.Lphi);
+                    if (L2) {
+                        #pragma unroll
+                        for (int j = 0; j < 16; ++j) y[j] = lut_act_s(y[j], L2);
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 16; ++j) y[j] = lut_act(y[j], a.Lphi);
+                    }
                 }
                 if (a.R) {
-                    const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
-                    #pragma unroll
-                    for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) y[j] = int(sat32(i64(y[j]) + __ldg(rp + j)));
+                    if (a.rvec && full16) {
+                        const int r16[16] = {rv[0].x, rv[0].y, rv[0].z, rv[0].w, rv[1].x, rv[1].y, rv[1].z, rv[1].w,
+                                             rv[2].x, rv[2].y, rv[2].z, rv[2].w, rv[3].x, rv[3].y, rv[3].z, rv[3].w};
+                        #pragma unroll
+                        for (int j = 0; j < 16; ++j) y[j] = int(sat32(i64(y[j]) + r16[j]));
+                    } else {
+                        const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
+                        #pragma unroll
+                        for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) y[j] = int(sat32(i64(y[j]) + __ldg(rp + j)));
+                    }
                 }
                 int32_t* dst = a.Y + size_t(grow) * a.ldy + n;
                 if (full16 && (a.ldy & 3) == 0) {
@@ -145,7 +178,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
                 int v[8];
                 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const int ge = lut_act(y[2 * j + 1], a.Lphi);
+                    const int ge = L2 ? lut_act_s(y[2 * j + 1], L2) : lut_act(y[2 * j + 1], a.Lphi);
                     v[j] = int(rshr_pos(i64(y[2 * j]) * ge, 16));
                     mx = max(mx, uabs(v[j]));
                 }

@@ -19,7 +19,7 @@
 
 namespace vela {
 
-template <int BN, int STAGES, int SRC> struct PersistCfg {
+template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static constexpr bool REG = SRC != SRC_I8;
     static constexpr int BM = 128, BK = 64;
     static constexpr int A_BYTES = BM * BK, W_BYTES = BN * BK;
@@ -29,22 +29,30 @@ template <int BN, int STAGES, int SRC> struct PersistCfg {
     static constexpr int TCOLS = ACC_BUFS * ACC_COLS;
     static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : (TCOLS <= 64 ? 64 : (TCOLS <= 128 ? 128 : (TCOLS <= 256 ? 256 : 512)));
     static constexpr int NCW = REG ? 8 : 0;
+    // epilogue warps: 16 (four per TMEM lane quarter) for planar sources, 8 where converters share the SM or a
+    // q|k|v head (64 columns) is one thread's unit
+    static constexpr int EW = (REG || EPI == EPI_QKV) ? 8 : 16;
+    static constexpr int NCOL = BN / (EW / 4);                 // columns of a tile per epilogue thread
     static constexpr int EPI_WARP0 = 2 + NCW;
-    static constexpr int THREADS = 32 * (2 + NCW + 8);
+    static constexpr int THREADS = 32 * (2 + NCW + EW);
     static constexpr int CTRL = 1024;
+    static constexpr bool SLUT = !REG;                          // GELU table staged in shared memory
+    static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [2][BN] column constants (double-buffered by tile)
+    static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[2048]
     static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
-    static constexpr int OFF_X = (STAGES * STAGE + CTRL + 1023) / 1024 * 1024;
+    static constexpr int OFF_X = (OFF_LUT + (SLUT ? 2048 * 8 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
     static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
     static constexpr int SMEM = 1024 + OFF_X + (X_STAGES > 0 ? X_STAGES : 0) * X_STAGE;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "MMA N");
+    static_assert(NCOL % 16 == 0 && (EPI != EPI_QKV || NCOL == 64), "epilogue column split");
     static_assert(STAGE % 1024 == 0, "stage alignment");
     static_assert(!REG || X_STAGES >= 2, "int32 sources need a staging ring of at least two stages");
 };
 
 template <int BN, int STAGES, int SRC, int EPI>
-__global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_persist_kernel(const __grid_constant__ GemmArgs a) {
-    using Cfg = PersistCfg<BN, STAGES, SRC>;
+__global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) gemm_persist_kernel(const __grid_constant__ GemmArgs a) {
+    using Cfg = PersistCfg<BN, STAGES, SRC, EPI>;
     constexpr bool REG = Cfg::REG;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -56,6 +64,8 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_
     uint64_t* xempty = xfull + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 4);
     uint8_t* xstage = smem + Cfg::OFF_X;
+    int4* s_cst = reinterpret_cast<int4*>(smem + Cfg::OFF_CST);
+    int2* s_lut = reinterpret_cast<int2*>(smem + Cfg::OFF_LUT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nN = (a.Np + BN - 1) / BN, nM = (a.Mp + Cfg::BM - 1) / Cfg::BM;
@@ -65,11 +75,13 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1 + Cfg::NCW); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 8); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], Cfg::EW); }
         for (int s = 0; s < 4; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], Cfg::NCW > 0 ? Cfg::NCW : 1); }
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
+    if (Cfg::SLUT && a.Lphi)
+        for (int i = threadIdx.x; i < 2048; i += blockDim.x) { const int x0 = __ldg(a.Lphi + i), x1 = __ldg(a.Lphi + i + 1); s_lut[i] = make_int2(x0, x1 - x0); }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&a.tmW);
         if (SRC == SRC_I8) { tma_prefetch_desc(&a.tmA_hi); tma_prefetch_desc(&a.tmA_lo); }
@@ -220,16 +232,29 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int ew = warp - Cfg::EPI_WARP0;            // 0..7
-        const int q = warp & 3, h = ew >> 2;             // TMEM lane quarter (fixed by warp % 4), column half
+        const int ew = warp - Cfg::EPI_WARP0;            // 0 .. EW-1
+        const int et = threadIdx.x - Cfg::EPI_WARP0 * 32;
+        const int q = warp & 3, hq = ew >> 2;            // TMEM lane quarter (fixed by warp % 4), column slice
         const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
+        const int2* lut = (Cfg::SLUT && a.Lphi) ? s_lut : nullptr;
+        bool ok = true;
         int tl = 0;
+        // Every epilogue warp runs every tile and every named barrier, also after a timed-out wait (it then skips
+        // the work), so no warp waits on a barrier that another one has left.
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             const int b = Cfg::ACC_BUFS == 2 ? (tl & 1) : 0, u = Cfg::ACC_BUFS == 2 ? (tl >> 1) : tl;
-            if (!__all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC))) break;
-            tc_fence_after();
             const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM, n0 = (r % nN) * BN;
-            gemm_epilogue<BN, SRC, EPI>(a, tq + uint32_t(b * Cfg::ACC_COLS), a.cst + n0, m0, n0, q * 32 + lane, h, z);
+            // this tile's column constants and the row exponent, fetched while the MMAs run
+            int4* cb = s_cst + (tl & 1) * BN;
+            for (int i = et; i < BN; i += Cfg::EW * 32) cb[i] = n0 + i < a.Np ? __ldg(a.cst + n0 + i) : make_int4(1, 0, 0, 0);
+            const int grow = m0 + q * 32 + lane;
+            int er = 0;
+            if (grow < a.Mreal) er = (SRC == SRC_X32) ? row_exp(__ldg(a.rowmax_in + grow)) : __ldg(a.e + grow);
+            asm volatile("bar.sync 2, %0;" :: "r"(Cfg::EW * 32) : "memory");
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC));
+            if (!ok) continue;
+            tc_fence_after();
+            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[b]);
@@ -242,7 +267,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC>::THREADS, 1) gemm_
 
 template <int BN, int STAGES, int SRC, int EPI>
 void launch_gemm_persist(const GemmArgs& a, cudaStream_t st) {
-    using Cfg = PersistCfg<BN, STAGES, SRC>;
+    using Cfg = PersistCfg<BN, STAGES, SRC, EPI>;
     auto kern = gemm_persist_kernel<BN, STAGES, SRC, EPI>;
     static int attr_done[64] = {0};
     const int dev = current_device();
