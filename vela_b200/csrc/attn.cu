@@ -18,8 +18,8 @@
 //       softmax warps as the A operand; A = Ph.Vh, Y = Ph.Vl + Pl.Vh, D = Pl.Vl (K-major V^T tiles);
 //       n = number of keys swept (padded keys carry V = 0 and P = 0).
 // Warp roles: warp 0 TMA (Q once; K tiles + per-key ek/ksum each pass; V^T tiles in pass 2),
-// warp 1 TMEM allocation + MMA issue, warps 2..9 softmax (thread = one query row = one TMEM
-// lane; the two warps of a lane quarter split each 64-key tile and the output dims).
+// warp 1 TMEM allocation + MMA issue, warps 2..17 softmax (thread = one query row = one TMEM
+// lane; the four warps of a lane quarter split each 64-key tile, and the output dims, in quarters).
 // TMEM: QK buffers at columns [0,192) and [192,384) (passes 0-1 alternate; pass 2 uses the first),
 // P.V accumulators at [192,384) during pass 2.  All barrier waits are bounded.
 #include "intops.cuh"
@@ -48,9 +48,11 @@ constexpr int OFF_P = OFF_V + VS * VSTAGE;
 constexpr int OFF_KAUX = OFF_P + 2 * P_BYTES;          // per K stage: ek int32[64], ksum int64[64]
 constexpr int KAUX_BYTES = 64 * 4 + 64 * 8;
 constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025]: (L[i], L[i+1] - L[i]); entry 1024 = (0, 0)
-constexpr int OFF_RED = OFF_LUT + 1032 * 8;            // cross-warp reductions: 2 x 128 x 8 bytes
-constexpr int OFF_WK = OFF_RED + 2 * 128 * 8;          // per softmax warp: ek[32], 128*ksum[32] of its keys
-constexpr int OFF_BAR = OFF_WK + 8 * 64 * 4;
+constexpr int SW = 16;                                 // softmax warps: four per TMEM lane quarter, 16 keys each
+constexpr int THREADS = 32 * (2 + SW);
+constexpr int OFF_RED = OFF_LUT + 1032 * 8;            // cross-warp reductions: 4 x 128 x 8 bytes
+constexpr int OFF_WK = OFF_RED + 4 * 128 * 8;          // per softmax warp: ek[16], 128*ksum[16] of its keys
+constexpr int OFF_BAR = OFF_WK + SW * 32 * 4;
 constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
 constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;
 constexpr int TMEM_COLS = 512;
@@ -86,81 +88,97 @@ __device__ __forceinline__ int lut_exp(uint32_t z, const int2* L2) {
     return e.x + int(((long long)e.y * int(z & 1023u)) >> 10);
 }
 
-// One 32-key half tile of one pass for one query row (this thread) -- scores from the three TMEM accumulators
+// One 16-key quarter tile of one pass for one query row (this thread) -- scores from the three TMEM accumulators
 // (HH at taddr, X at +64, LL at +128), then PASS 0: row max; PASS 1: sum of E; PASS 2: P (into pw_h / pw_l).
 template <int PASS>
-__device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ wk, int shq, int r0, int cq, bool fast, bool full,
-                                             int kbase, int q, int Tk, int causal, const int2* __restrict__ L2,
+__device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ wk, int shq, int r0, int cq, bool fast, bool unif, int eku,
+                                             bool full, int kbase, int q, int Tk, int causal, const int2* __restrict__ L2,
                                              int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l) {
-    #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        int hh[16], xx[16], ll[16];
-        tmem_ld16(taddr + c * 16, hh); tmem_ld16(taddr + c * 16 + 64, xx); tmem_ld16(taddr + c * 16 + 128, ll);
+    // X and LL first, folded into T (16 registers), then HH: the three accumulators are never all live at once
+    int s[16];
+    {
+        int xx[16], ll[16];
+        tmem_ld16(taddr + 64, xx); tmem_ld16(taddr + 128, ll);
         tmem_ld_wait();
-        int s[16];
-        if (fast) {
+        if (fast && unif) {
+            const int cr = cq + (r0 >> eku);       // one key exponent for the chunk: rounding term of shift shq - eku
             #pragma unroll
             for (int u = 0; u < 16; u += 4) {
-                const int4 e4 = *reinterpret_cast<const int4*>(wk + c * 16 + u);
-                const int4 k4 = *reinterpret_cast<const int4*>(wk + 32 + c * 16 + u);
-                const int ek[4] = {e4.x, e4.y, e4.z, e4.w}, kc[4] = {k4.x, k4.y, k4.z, k4.w};
-                #pragma unroll
-                for (int w = 0; w < 4; ++w)
-                    s[u + w] = score_fast(hh[u + w], (xx[u + w] << 8) + ll[u + w] + (cq + kc[w]) + (r0 >> ek[w]), shq - ek[w]);
+                const int4 k4 = *reinterpret_cast<const int4*>(wk + 16 + u);
+                s[u] = (xx[u] << 8) + (ll[u] + k4.x + cr); s[u + 1] = (xx[u + 1] << 8) + (ll[u + 1] + k4.y + cr);
+                s[u + 2] = (xx[u + 2] << 8) + (ll[u + 2] + k4.z + cr); s[u + 3] = (xx[u + 3] << 8) + (ll[u + 3] + k4.w + cr);
             }
+        } else if (fast) {
+            #pragma unroll
+            for (int u = 0; u < 16; u += 4) {
+                const int4 e4 = *reinterpret_cast<const int4*>(wk + u);
+                const int4 k4 = *reinterpret_cast<const int4*>(wk + 16 + u);
+                s[u] = (xx[u] << 8) + (ll[u] + k4.x + cq) + (r0 >> e4.x); s[u + 1] = (xx[u + 1] << 8) + (ll[u + 1] + k4.y + cq) + (r0 >> e4.y);
+                s[u + 2] = (xx[u + 2] << 8) + (ll[u + 2] + k4.z + cq) + (r0 >> e4.z); s[u + 3] = (xx[u + 3] << 8) + (ll[u + 3] + k4.w + cq) + (r0 >> e4.w);
+            }
+        } else {
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) s[u] = (xx[u] << 8) + ll[u] + cq + wk[16 + u];
+        }
+    }
+    {
+        int hh[16];
+        tmem_ld16(taddr, hh);
+        tmem_ld_wait();
+        if (fast && unif) {
+            const int sh = shq - eku;
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) s[u] = score_fast(hh[u], s[u], sh);
+        } else if (fast) {
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) s[u] = score_fast(hh[u], s[u], shq - wk[u]);
         } else {            // a shift outside [5, 19] somewhere in the tile: the 64-bit rshr with saturation
             #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int ek = wk[c * 16 + u], kc = wk[32 + c * 16 + u];
-                s[u] = int(rshr((i64(hh[u]) << 16) + ((xx[u] << 8) + ll[u] + cq + kc), shq - ek));
-            }
+            for (int u = 0; u < 16; ++u) s[u] = int(rshr((i64(hh[u]) << 16) + s[u], shq - wk[u]));
         }
-        uint32_t vmask = 0xFFFFu;   // validity by key position (a valid score may itself saturate to INT_MIN)
+    }
+    uint32_t vmask = 0xFFFFu;   // validity by key position (a valid score may itself saturate to INT_MIN)
+    if (!full) {
+        vmask = 0;
+        #pragma unroll
+        for (int u = 0; u < 16; ++u) { const int key = kbase + u; vmask |= uint32_t(key < Tk && !(causal && key > q)) << u; }
+    }
+    if constexpr (PASS == 0) {
         if (!full) {
-            vmask = 0;
             #pragma unroll
-            for (int u = 0; u < 16; ++u) { const int key = kbase + c * 16 + u; vmask |= uint32_t(key < Tk && !(causal && key > q)) << u; }
+            for (int u = 0; u < 16; ++u) s[u] = (vmask >> u) & 1u ? s[u] : INT_MIN;
         }
-        if constexpr (PASS == 0) {
-            if (!full) {
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) s[u] = (vmask >> u) & 1u ? s[u] : INT_MIN;
-            }
+        #pragma unroll
+        for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
+    } else if constexpr (PASS == 1) {
+        // each E < 2^31 (the table holds int32 values >= 0): a pair fits 32 bits
+        #pragma unroll
+        for (int u = 0; u < 16; u += 2) {
+            uint32_t e0 = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u]), L2)), e1 = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u + 1]), L2));
+            if (!full) { e0 = (vmask >> u) & 1u ? e0 : 0u; e1 = (vmask >> (u + 1)) & 1u ? e1 : 0u; }
+            sum += e0 + e1;
+        }
+    } else {
+        // P = min(32767, (E r + 2^46) >> 47) with r = rhi 2^32 + rlo.  E <= sum E, so E r <= 2^62 and
+        // floor(E r / 2^32) = E rhi + umulhi(E, rlo) <= 2^30 fits 32 bits.  Four keys at a time, packed at once.
+        #pragma unroll
+        for (int u = 0; u < 16; u += 4) {
+            int P[4];
             #pragma unroll
-            for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
-        } else {
-            int E[16];
-            #pragma unroll
-            for (int u = 0; u < 16; ++u) E[u] = lut_exp(uint32_t(mx) - uint32_t(s[u]), L2);
-            if (!full) {
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) E[u] = (vmask >> u) & 1u ? E[u] : 0;
+            for (int w = 0; w < 4; ++w) {
+                uint32_t e = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u + w]), L2));
+                if (!full) e = (vmask >> (u + w)) & 1u ? e : 0u;
+                const uint32_t h = e * rhi + (__umulhi(e, rlo) + 16384u);
+                P[w] = int(min(32767u, h >> 15));
+                psum += P[w];
             }
-            if constexpr (PASS == 1) {
-                // each E < 2^31 (the table holds int32 values >= 0): a pair fits 32 bits
-                #pragma unroll
-                for (int u = 0; u < 16; u += 2) sum += uint32_t(E[u]) + uint32_t(E[u + 1]);
-            } else {
-                // P = min(32767, (E r + 2^46) >> 47) with r = rhi 2^32 + rlo.  E <= sum E, so E r <= 2^62 and
-                // floor(E r / 2^32) = E rhi + umulhi(E, rlo) <= 2^30 fits 32 bits.
-                int P[16];
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const uint32_t h = uint32_t(E[u]) * rhi + __umulhi(uint32_t(E[u]), rlo);
-                    P[u] = int(min(32767u, (h + 16384u) >> 15));
-                    psum += P[u];
-                }
-                #pragma unroll
-                for (int u = 0; u < 16; u += 4) {
-                    pw_h[c * 4 + u / 4] = pack_hi4(P[u], P[u + 1], P[u + 2], P[u + 3]);
-                    pw_l[c * 4 + u / 4] = pack_lo4(P[u], P[u + 1], P[u + 2], P[u + 3]);
-                }
-            }
+            pw_h[u / 4] = pack_hi4(P[0], P[1], P[2], P[3]);
+            pw_l[u / 4] = pack_lo4(P[0], P[1], P[2], P[3]);
         }
     }
 }
 
-__global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
@@ -179,10 +197,10 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < KS; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1 + 8); }
+        for (int s = 0; s < KS; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1 + SW); }
         for (int s = 0; s < VS; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&qk_full[b], 1); mbar_init(&qk_free[b], 8); }
-        mbar_init(p_full, 8); mbar_init(p_free, 1); mbar_init(pv_done, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(&qk_full[b], 1); mbar_init(&qk_free[b], SW); }
+        mbar_init(p_full, SW); mbar_init(p_free, 1); mbar_init(pv_done, 1);
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
@@ -228,7 +246,6 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + Q_BYTES;
             const uint32_t ph = smem_u32(sm + OFF_P), pl = ph + P_BYTES;
             const uint32_t pv = tmem + 192;                   // A: [192,256), Y: [256,320), D: [320,384)
-            int uses[2] = {0, 0};
             bool ok = mbar_wait(q_full, 0, a.err, DEVERR_TIMEOUT_FULL);
             auto issue_pv = [&](int j) -> bool {
                 const int vs = j % VS;
@@ -251,11 +268,13 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             for (int it = 0; it < nIt && ok; ++it) {
                 const int pass = it / nT, j = it % nT, ks = it % KS;
                 const int b = pass < 2 ? (it & 1) : 0;
-                if (pass == 2 && j == 0 && uses[1] > 0) {      // the P.V accumulators reuse buffer 1's columns
-                    if (!mbar_wait(&qk_free[1], (uses[1] & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                // earlier uses of buffer b: passes 0-1 alternate the buffers, pass 2 keeps buffer 0
+                const int ub = it < 2 * nT ? (it >> 1) : it - nT;
+                if (pass == 2 && j == 0) {      // the P.V accumulators reuse buffer 1's columns (used nT times)
+                    if (!mbar_wait(&qk_free[1], (nT & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
                 }
                 if (!mbar_wait(&k_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL)) { ok = false; break; }
-                if (!mbar_wait(&qk_free[b], (uses[b] & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                if (!mbar_wait(&qk_free[b], (ub & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t kh = smem_u32(sm + OFF_K + ks * KSTAGE), kl = kh + KT_BYTES;
                 const uint32_t d = tmem + b * 192;
@@ -268,7 +287,6 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
                 }
                 mma_commit(&qk_full[b]);
                 mma_commit(&k_empty[ks]);
-                ++uses[b];
                 if (pass == 2 && j >= 1) ok = issue_pv(j - 1);
             }
             if (ok) ok = issue_pv(nT - 1);
@@ -276,7 +294,7 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         }
     } else {
         // ---------------------------------------------------------------- softmax / output warps
-        const int qq = warp & 3, half = (warp - 2) >> 2;           // lane quarter, key half (and dim half)
+        const int qq = warp & 3, kq = (warp - 2) >> 2;             // lane quarter; key quarter (and dim quarter)
         const int rl = qq * 32 + lane, q = q0 + rl;
         const uint32_t tl = uint32_t(qq * 32) << 16;
         const size_t rq = size_t(g) * a.Tqp + q;
@@ -285,10 +303,9 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
         const int shq = 19 - eqv;                                   // eq <= 17, so shq >= 2
         const int r0 = 1 << (shq - 1);                              // rounding term of shift shq; >> ek gives that of shq - ek
         const int shq_min = __reduce_min_sync(0xffffffffu, shq);
-        int* wk = reinterpret_cast<int*>(sm + OFF_WK) + (warp - 2) * 64;
-        i64* red = reinterpret_cast<i64*>(sm + OFF_RED);          // [2][128]
+        int* wk = reinterpret_cast<int*>(sm + OFF_WK) + (warp - 2) * 32;
+        i64* red = reinterpret_cast<i64*>(sm + OFF_RED);          // [4][128]
         int mx = INT_MIN; uint64_t sum = 0; uint32_t rlo = 0, rhi = 0; int psum = 0;
-        int uses[2] = {0, 0};
         bool ok = true;
         // Every warp runs all iterations and every named barrier, also after a timed-out wait
         // (then it skips the work), so no warp can be left waiting on a barrier the others skipped.
@@ -296,25 +313,27 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             for (int j = 0; j < nT; ++j) {
                 const int it = pass * nT + j, ks = it % KS;
                 const int b = pass < 2 ? (it & 1) : 0;
-                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], uses[b] & 1, a.err, DEVERR_TIMEOUT_FULL));
-                ++uses[b];
+                const int ub = it < 2 * nT ? (it >> 1) : it - nT;      // earlier uses of buffer b
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL));
                 if (ok) {
                     tc_fence_after();
-                    // this warp's 32 keys: exponent and 128 * ksum, staged once per tile for vector reads
+                    // this warp's 16 keys: exponent and 128 * ksum, staged once per tile for vector reads
                     const uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
-                    const int ekL = reinterpret_cast<const int32_t*>(aux)[half * 32 + lane];
-                    const int kcL = int(128 * reinterpret_cast<const i64*>(aux + 256)[half * 32 + lane]);
-                    const int emax = __reduce_max_sync(0xffffffffu, ekL);
-                    wk[lane] = ekL; wk[32 + lane] = kcL;
+                    const int kk = kq * 16 + (lane & 15);
+                    const int ekL = reinterpret_cast<const int32_t*>(aux)[kk];
+                    const int kcL = int(128 * reinterpret_cast<const i64*>(aux + 256)[kk]);
+                    const int emax = __reduce_max_sync(0xffffffffu, ekL), emin = __reduce_min_sync(0xffffffffu, ekL);
+                    if (lane < 16) { wk[lane] = ekL; wk[16 + lane] = kcL; }
                     __syncwarp();
-                    const int kbase = j * 64 + half * 32;
-                    const bool full = !a.causal && kbase + 32 <= a.Tk;
+                    const int kbase = j * 64 + kq * 16;
+                    const bool full = !a.causal && kbase + 16 <= a.Tk;
                     const bool fast = shq_min - emax >= 5;           // every shift of the tile in [5, 19]
-                    const uint32_t taddr = tmem + tl + uint32_t(b * 192 + half * 32);
-                    uint32_t pw_h[8], pw_l[8];                        // P bytes of this thread's 32 keys (pass 2)
-                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
-                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
-                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    const uint32_t taddr = tmem + tl + uint32_t(b * 192 + kq * 16);
+                    uint32_t pw_h[4], pw_l[4];                        // P bytes of this thread's 16 keys (pass 2)
+                    const bool unif = emin == emax;
+                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
+                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
                     // this warp is done with the QK buffer, the K stage's per-key data and its key staging
                     tc_fence_before();
                     __syncwarp();
@@ -323,24 +342,24 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
                         ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
                         if (ok) {
                             uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
-                            *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
-                            *reinterpret_cast<uint4*>(php + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_h[4], pw_h[5], pw_h[6], pw_h[7]);
-                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2)) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
-                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, half * 2 + 1)) = make_uint4(pw_l[4], pw_l[5], pw_l[6], pw_l[7]);
+                            *reinterpret_cast<uint4*>(php + sw64_off(rl, kq)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
+                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, kq)) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
                             fence_async_smem();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(p_full);
                         }
                     }
                 }
-                if (j == nT - 1 && pass < 2) {         // combine the two key halves of each row
-                    red[half * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
-                    asm volatile("bar.sync 1, 256;" ::: "memory");
-                    const i64 other = red[(half ^ 1) * 128 + rl];
-                    asm volatile("bar.sync 1, 256;" ::: "memory");
-                    if (pass == 0) mx = max(mx, int(other));
+                if (j == nT - 1 && pass < 2) {         // combine the four key quarters of each row
+                    red[kq * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
+                    asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
+                    i64 o[3];
+                    #pragma unroll
+                    for (int w = 1; w < 4; ++w) o[w - 1] = red[((kq + w) & 3) * 128 + rl];
+                    asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
+                    if (pass == 0) mx = max(max(mx, int(o[0])), max(int(o[1]), int(o[2])));
                     else {
-                        const uint64_t tot = sum + uint64_t(other);
+                        const uint64_t tot = sum + uint64_t(o[0]) + uint64_t(o[1]) + uint64_t(o[2]);
                         const uint64_t r = tot ? (uint64_t(1) << 62) / tot : 0;
                         rlo = uint32_t(r); rhi = uint32_t(r >> 32);
                     }
@@ -348,9 +367,9 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             }
         }
         // ---------------------------------------------------------------- output
-        red[half * 128 + rl] = psum;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        const i64 ps = i64(psum) + red[(half ^ 1) * 128 + rl];
+        red[kq * 128 + rl] = psum;
+        asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
+        const i64 ps = red[rl] + red[128 + rl] + red[256 + rl] + red[384 + rl];
         const bool done = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC));
         tc_fence_after();
         if (done) {
@@ -358,23 +377,23 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ At
             const i64 n = a.Tkp;
             u32 am = 0;
             #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                int A[16], Y[16], D[16];
-                const uint32_t col = uint32_t(192 + half * 32 + c * 16);
-                tmem_ld16(tmem + tl + col, A); tmem_ld16(tmem + tl + col + 64, Y); tmem_ld16(tmem + tl + col + 128, D);
+            for (int hv = 0; hv < 2; ++hv) {           // two halves of 8 output dims: fewer live registers
+                int A[8], Y[8], D[8];
+                const uint32_t col = uint32_t(192 + kq * 16 + hv * 8);
+                tmem_ld8(tmem + tl + col, A); tmem_ld8(tmem + tl + col + 64, Y); tmem_ld8(tmem + tl + col + 128, D);
                 tmem_ld_wait();
                 if (q < a.Tq) {
-                    int o[16];
+                    int o[8];
                     #pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        const int dd = half * 32 + c * 16 + u;
+                    for (int u = 0; u < 8; ++u) {
+                        const int dd = kq * 16 + hv * 8 + u;
                         const i64 O = 65536 * i64(A[u]) + 256 * i64(Y[u]) + D[u] + 128 * (ps + __ldg(a.vsum + g * 64 + dd)) - 16384 * n;
                         o[u] = int(rshr(O, 15 - __ldg(a.ev + g * 64 + dd)));
                         am = max(am, uabs(o[u]));
                     }
-                    int32_t* dst = a.out + (size_t(bidx) * a.Tq + q) * a.C + h * 64 + half * 32 + c * 16;
-                    #pragma unroll
-                    for (int u = 0; u < 16; u += 4) *reinterpret_cast<int4*>(dst + u) = make_int4(o[u], o[u + 1], o[u + 2], o[u + 3]);
+                    int32_t* dst = a.out + (size_t(bidx) * a.Tq + q) * a.C + h * 64 + kq * 16 + hv * 8;
+                    *reinterpret_cast<int4*>(dst) = make_int4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<int4*>(dst + 4) = make_int4(o[4], o[5], o[6], o[7]);
                 }
             }
             if (a.rowmax && q < a.Tq && am) atomicMax(a.rowmax + size_t(bidx) * a.Tq + q, am);
@@ -412,7 +431,7 @@ void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, cons
         VELA_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         if (dev < 64) attr_done[dev] = 1;
     }
-    attn_kernel<<<dim3(ceil_div(Tqp, 128), G), 320, SMEM, st>>>(a);
+    attn_kernel<<<dim3(ceil_div(Tqp, 128), G), THREADS, SMEM, st>>>(a);
     VELA_CUDA(cudaGetLastError());
 }
 }  // namespace vela
