@@ -64,11 +64,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu", "norms"], default=None,
                     help="run only the named kernel(s) at the BASELINE config shape (attention: config 2, gemm: config 1, "
                          "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 for 640 ch 32x32 / 1280 ch 16x16), "
                          "linear: the UNet's int32-input linear with residual at 64x64 (M 32768, K --linear-k, N 320), "
-                         "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); "
+                         "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); norms: GroupNorm statistics, "
+                         "GroupNorm+SiLU apply and LayerNorm->planes at 320 ch 64x64, each timed alone; "
                          "print their CUDA-event times as one JSON line and exit")
     ap.add_argument("--linear-k", type=int, default=320)
     ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2])
@@ -349,6 +350,24 @@ class GnConvCase:
     def launch(self):
         self.gn(); self.conv()
 
+    def report_norms(self):
+        """GroupNorm statistics, GroupNorm + SiLU apply (int32 + pixel max) and LayerNorm -> planes, timed apart"""
+        import torch
+        B, Hh, C, T, N, K = self.dims
+        st, P = self.stream.cuda_stream, self.P
+        stats = lambda: self.V.check(self.L.vela_gn_stats(st, P(self.X), B, T, C, 32, 100000, P(self.gs)))
+        apply = lambda: self.V.check(self.L.vela_gn_apply_row(st, P(self.X), B, T, C, 32, P(self.gs), P(self.gam), P(self.beta), P(self.Lsig),
+                                                               P(self.Y), P(self.pm), None, None, None, 0))
+        stats()
+        hi = torch.empty((B * T, C), dtype=torch.int8, device=self.X.device); lo = torch.empty_like(hi)
+        e = torch.empty((B * T,), dtype=torch.int32, device=self.X.device)
+        ln = lambda: self.V.check(self.L.vela_lnorm_q(st, P(self.X), B * T, C, P(self.gam), P(self.beta), 100000, P(hi), P(lo), P(e), C))
+        ts, ta, tl = _time_ms(self.stream, stats), _time_ms(self.stream, apply), _time_ms(self.stream, ln)
+        nb = B * T * C * 4
+        return {"kernel": "norms (320 ch 64x64)", "gn_stats_ms": round(ts, 4), "gn_stats_gbs": round(2 * nb / ts / 1e6, 1),
+                "gn_apply_ms": round(ta, 4), "gn_apply_gbs": round((2 * nb + B * T * 4) / ta / 1e6, 1),
+                "lnorm_q_ms": round(tl, 4), "lnorm_q_gbs": round((nb + nb // 2) / tl / 1e6, 1)}
+
     def report(self):
         B, Hh, C, T, N, K = self.dims
         self.gn()
@@ -614,6 +633,9 @@ def run_kernel(a, R):
     elif a.kernel == "gemm":
         case = GemmCase(dev)
         rep = case.report()
+    elif a.kernel == "norms":
+        case = GnConvCase(dev, 0)
+        rep = case.report_norms()
     elif a.kernel in ("linear", "geglu"):
         case = LinearCase(dev, a.kernel, a.linear_k if a.kernel == "linear" else 320)
         rep = case.report()

@@ -32,6 +32,15 @@ __device__ __forceinline__ i64 floor_div_inv(i64 a, uint64_t d, uint64_t inv) {
     return r ? -i64(q) - 1 : -i64(q);
 }
 
+// lut_act (intops.cuh) with the table staged in shared memory as (L[i], L[i+1] - L[i])
+__device__ __forceinline__ int lut_act_smem(int x, const int2* __restrict__ L2) {
+    int l;
+    if (x < -(16 << 16)) l = 0;
+    else if (x >= (16 << 16)) l = 65536;
+    else { const int z = x + (16 << 16); const int2 t = L2[z >> 10]; l = t.x + ((t.y * (z & 1023)) >> 10); }
+    return int(rshr_pos(i64(x) * l, 16));
+}
+
 // 16 quantised values of one row written as hi / lo bytes at column c (c % 4 == 0)
 __device__ __forceinline__ void store_q4(int8_t* hi, int8_t* lo, int c, int q0, int q1, int q2, int q3) {
     *reinterpret_cast<u32*>(hi + c) = pack_hi4(q0, q1, q2, q3);
@@ -104,40 +113,11 @@ __global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restr
 }
 
 // ---------------------------------------------------------------- GroupNorm (src/kernels.cu:173-221,285-305,420-487)
-// Per-(sample, group) accumulation record = vela_gnstat {sum, mn, mx, mean, e, ss, sd}.
-// Pass 1: block = (row chunk, sample); thread = one channel quad for all rows of the chunk (coalesced
-// row-major reads), per-channel sums in registers, then one smem and one global atomic per group.
+// Per-(sample, group) accumulation record = vela_gnstat {sum, mn, mx, mean, e, ss, sd}: zeroed, then the two
+// statistics passes accumulate into it with atomics, then the finish kernel derives mean, e and sd.
 __global__ void gn_init_kernel(vela_gnstat* gs, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) { gs[i].sum = 0; gs[i].mn = INT_MAX; gs[i].mx = INT_MIN; gs[i].mean = 0; gs[i].e = 0; gs[i].pad_ = 0; gs[i].ss = 0; gs[i].sd = 0; }
-}
-__global__ void gn_pass1_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
-    __shared__ long long ssum[32]; __shared__ int smn[32], smx[32];
-    const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock), C4 = C >> 2, cg = C >> 5;
-    if (threadIdx.x < 32) { ssum[threadIdx.x] = 0; smn[threadIdx.x] = INT_MAX; smx[threadIdx.x] = INT_MIN; }
-    __syncthreads();
-    for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
-        i64 s[4] = {0, 0, 0, 0}; int mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
-        const int32_t* x = X + (size_t(b) * T + t0) * C + c4 * 4;
-        for (int t = t0; t < t1; ++t, x += C) {
-            const int4 v = __ldg(reinterpret_cast<const int4*>(x));
-            s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
-            mn[0] = min(mn[0], v.x); mn[1] = min(mn[1], v.y); mn[2] = min(mn[2], v.z); mn[3] = min(mn[3], v.w);
-            mx[0] = max(mx[0], v.x); mx[1] = max(mx[1], v.y); mx[2] = max(mx[2], v.z); mx[3] = max(mx[3], v.w);
-        }
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int g = (c4 * 4 + k) / cg;
-            atomicAdd(reinterpret_cast<unsigned long long*>(&ssum[g]), (unsigned long long)s[k]);
-            atomicMin(&smn[g], mn[k]); atomicMax(&smx[g], mx[k]);
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x < 32 && t1 > t0) {
-        vela_gnstat* st = gs + b * 32 + threadIdx.x;
-        atomicAdd(reinterpret_cast<unsigned long long*>(&st->sum), (unsigned long long)ssum[threadIdx.x]);
-        atomicMin(&st->mn, smn[threadIdx.x]); atomicMax(&st->mx, smx[threadIdx.x]);
-    }
 }
 // mean and exponent of one group, src/kernels.cu:185-191
 __device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean, int& e) {
@@ -145,27 +125,65 @@ __device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean
     const i64 m = max(i64(s.mx) - mean, mean - i64(s.mn));
     e = max(0, (m >= (i64(1) << 32) ? 17 : row_exp(u32(m))) - 5);
 }
-__global__ void gn_pass2_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
-    __shared__ long long sss[32]; __shared__ long long smean[32]; __shared__ int se[32];
-    const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock), C4 = C >> 2, cg = C >> 5;
-    if (threadIdx.x < 32) { i64 mean; int e; gn_mean_e(gs[b * 32 + threadIdx.x], i64(T) * cg, mean, e); smean[threadIdx.x] = mean; se[threadIdx.x] = e; sss[threadIdx.x] = 0; }
-    __syncthreads();
-    for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
-        int g[4]; i64 mean[4]; int e[4]; i64 ss[4] = {0, 0, 0, 0};
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) { g[k] = (c4 * 4 + k) / cg; mean[k] = smean[g[k]]; e[k] = se[g[k]]; }
-        const int32_t* x = X + (size_t(b) * T + t0) * C + c4 * 4;
-        for (int t = t0; t < t1; ++t, x += C) {
-            const int4 v = __ldg(reinterpret_cast<const int4*>(x));
-            const int vv[4] = {v.x, v.y, v.z, v.w};
-            #pragma unroll
-            for (int k = 0; k < 4; ++k) { const i64 d = i64(vv[k]) - mean[k]; const i64 dd = e[k] ? ((d >> e[k]) + ((d >> (e[k] - 1)) & 1)) : d; ss[k] += dd * dd; }
-        }
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) atomicAdd(reinterpret_cast<unsigned long long*>(&sss[g[k]]), (unsigned long long)ss[k]);
+// Statistics passes.  Block = Q x RP threads (Q = C / 4 column quads, RP row lanes); a thread keeps one quad
+// (four channels, fixed groups) over every RP-th row of the block's rows, four rows in flight, then the block
+// combines per group in shared memory and adds to the (sample, group) record once.
+template <int PASS>
+__global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
+    __shared__ long long sacc[32]; __shared__ int smn[32], smx[32]; __shared__ long long smean[32]; __shared__ int se[32];
+    const int Q = C >> 2, RP = blockDim.x / Q, cg = C >> 5;
+    const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock);
+    if (threadIdx.x < 32) {
+        sacc[threadIdx.x] = 0; smn[threadIdx.x] = INT_MAX; smx[threadIdx.x] = INT_MIN;
+        if (PASS == 2) { i64 mean; int e; gn_mean_e(gs[b * 32 + threadIdx.x], i64(T) * cg, mean, e); smean[threadIdx.x] = mean; se[threadIdx.x] = e; }
     }
     __syncthreads();
-    if (threadIdx.x < 32 && t1 > t0) atomicAdd(reinterpret_cast<unsigned long long*>(&gs[b * 32 + threadIdx.x].ss), (unsigned long long)sss[threadIdx.x]);
+    const int c4 = threadIdx.x % Q, rr = threadIdx.x / Q;
+    if (rr < RP) {
+        const int c = c4 * 4;
+        int gi[4]; i64 mean[4] = {0, 0, 0, 0}; int e[4] = {0, 0, 0, 0};
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) { gi[k] = (c + k) / cg; if (PASS == 2) { mean[k] = smean[gi[k]]; e[k] = se[gi[k]]; } }
+        i64 acc[4] = {0, 0, 0, 0}; int mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+        const int32_t* x = X + (size_t(b) * T) * C + c;
+        auto take = [&](const int4 v) {
+            const int vv[4] = {v.x, v.y, v.z, v.w};
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (PASS == 1) { acc[k] += vv[k]; mn[k] = min(mn[k], vv[k]); mx[k] = max(mx[k], vv[k]); }
+                else { const i64 d = i64(vv[k]) - mean[k]; const i64 dd = e[k] ? ((d >> e[k]) + ((d >> (e[k] - 1)) & 1)) : d; acc[k] += dd * dd; }
+            }
+        };
+        int t = t0 + rr;
+        for (; t + 3 * RP < t1; t += 4 * RP) {
+            const int4 v0 = __ldg(reinterpret_cast<const int4*>(x + size_t(t) * C));
+            const int4 v1 = __ldg(reinterpret_cast<const int4*>(x + size_t(t + RP) * C));
+            const int4 v2 = __ldg(reinterpret_cast<const int4*>(x + size_t(t + 2 * RP) * C));
+            const int4 v3 = __ldg(reinterpret_cast<const int4*>(x + size_t(t + 3 * RP) * C));
+            take(v0); take(v1); take(v2); take(v3);
+        }
+        for (; t < t1; t += RP) take(__ldg(reinterpret_cast<const int4*>(x + size_t(t) * C)));
+        // channels of one group within the quad first (groups of >= 4 channels: at most two groups per quad)
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (k > 0 && gi[k] == gi[k - 1]) continue;
+            i64 a = acc[k]; int lo = mn[k], hi = mx[k];
+            #pragma unroll
+            for (int k2 = k + 1; k2 < 4; ++k2) if (gi[k2] == gi[k]) { a += acc[k2]; lo = min(lo, mn[k2]); hi = max(hi, mx[k2]); }
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sacc[gi[k]]), (unsigned long long)a);
+            if (PASS == 1) { atomicMin(&smn[gi[k]], lo); atomicMax(&smx[gi[k]], hi); }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 32 && t1 > t0) {
+        vela_gnstat* st = gs + b * 32 + threadIdx.x;
+        if (PASS == 1) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&st->sum), (unsigned long long)sacc[threadIdx.x]);
+            atomicMin(&st->mn, smn[threadIdx.x]); atomicMax(&st->mx, smx[threadIdx.x]);
+        } else {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&st->ss), (unsigned long long)sacc[threadIdx.x]);
+        }
+    }
 }
 // mean, e, ss -> var, eps, sd (src/kernels.cu:204-211)
 __global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den) {
@@ -180,80 +198,105 @@ __global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den) {
     s.sd = isqrt((var + eps) << 16);
     gs[i] = s;
 }
-// normalise one value: sat32(rshr(floor((d * 2^(24-e) * 2 + sd) / (2 sd)) * g, 16) + beta)
-__device__ __forceinline__ int norm_val(int x, i64 mean, int e, i64 sd, uint64_t inv, int g, int beta) {
-    const i64 d = i64(x) - mean;
-    const i64 yy = floor_div_inv(d * (i64(1) << (25 - e)) + sd, uint64_t(2 * sd), inv);
-    return int(sat32(rshr_pos(yy * g, 16) + beta));
+// Normalisation constants of one (sample, group) or one row, for the exact binary64 division of norm_val.
+struct NormP { double mean, scale, sd, D, rcp; };
+__device__ __forceinline__ NormP norm_params(i64 mean, int e, i64 sd) {
+    NormP p;
+    p.mean = double(mean); p.scale = double(i64(1) << (25 - e)); p.sd = double(sd); p.D = 2.0 * double(sd); p.rcp = 1.0 / p.D;
+    return p;
 }
-// Apply: one warp per row, 8 rows per block.  Mean, e, sd and the reciprocal of 2*sd of the 32 groups
-// are staged in shared memory: once per block when T % 8 == 0 (a block then never straddles two
-// samples), else once per warp.
-// R4 = int4 chunks per lane held in registers for the quantised output (C <= 128 * R4).
-template <int R4, bool QUANT>
-__global__ void gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs,
-                                const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
-                                int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
-    __shared__ long long sm_mean[8][32], sm_sd[8][32]; __shared__ unsigned long long sm_inv[8][32]; __shared__ int sm_e[8][32];
-    const int lane = threadIdx.x & 31, r = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const bool perBlock = (T & 7) == 0;
-    const int slot = perBlock ? 0 : (threadIdx.x >> 5);
-    if (perBlock ? threadIdx.x < 32 : r < M) {
-        const int bb = perBlock ? (blockIdx.x * 8) / T : r / T;
-        const vela_gnstat st = gs[bb * 32 + lane];
-        sm_mean[slot][lane] = st.mean; sm_e[slot][lane] = st.e; sm_sd[slot][lane] = st.sd;
-        sm_inv[slot][lane] = st.sd > 0 ? ~0ull / uint64_t(2 * st.sd) : 0ull;
+// normalise one value: sat32(rshr(floor((d * 2^(25-e) + sd) / (2 sd)) * g, 16) + beta), d = x - mean.
+// The quotient is formed in binary64, where every intermediate is an integer below 2^53: |d| <= the group's
+// range m < 2^(20+e) (2^33 when e = 12), so |d 2^(25-e)| < 2^46; the rounded product with the rounded 1/(2 sd)
+// is within 2^-6 of the true quotient, so one exact residual test (fma) corrects its floor.  sd >= 1 always
+// (sd = 0 would need var + eps = 0, impossible: a constant group has e = 0 and eps > 0).
+__device__ __forceinline__ int norm_val(int x, const NormP& p, int g, int beta) {
+    const double num = fma(double(x) - p.mean, p.scale, p.sd);
+    double q = floor(num * p.rcp);
+    const double r = fma(-q, p.D, num);
+    if (r < 0.0) q -= 1.0;
+    else if (r >= p.D) q += 1.0;
+    return int(sat32(rshr_pos(i64(q) * g, 16) + beta));
+}
+// Apply.  Block = PT x RP threads over rowsPerBlock consecutive rows, GN_RPT rows per thread: a thread owns a
+// channel pair (int2; pairs cover the row with stride PT = min(C/2, 1024)); the pair's group constants
+// (one group unless C/32 is odd and the pair straddles two) of the samples the block touches (at most GN_SPAN)
+// are staged in shared memory, g / beta stay in registers, the SiLU table is staged as (L[i], L[i+1] - L[i]),
+// and the pixel max of each row is combined with shared-memory atomics.  QUANT (C <= 2048): the rows stay in
+// registers until their maxima give the exponents, then hi / lo planes are written.
+constexpr int GN_RPT = 8, GN_SPAN = 4;
+template <bool QUANT>
+__global__ void __launch_bounds__(1024) gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs,
+                                                        const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
+                                                        int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                                                        int32_t* __restrict__ e, int Kp, int rowsPerBlock) {
+    __shared__ int2 s_lut[2048];
+    __shared__ NormP s_p[GN_SPAN][32];
+    __shared__ u32 s_rmax[256];
+    const int P2 = C >> 1, PT = min(P2, 1024), RP = blockDim.x / PT, cg = C >> 5;
+    const int r0 = blockIdx.x * rowsPerBlock, r1 = min(M, r0 + rowsPerBlock), b0 = r0 / T;
+    if (Lsig) for (int i = threadIdx.x; i < 2048; i += blockDim.x) { const int x0 = __ldg(Lsig + i), x1 = __ldg(Lsig + i + 1); s_lut[i] = make_int2(x0, x1 - x0); }
+    for (int i = threadIdx.x; i < rowsPerBlock; i += blockDim.x) s_rmax[i] = 0;
+    for (int i = threadIdx.x; i < GN_SPAN * 32; i += blockDim.x) {
+        const int sb = b0 + (i >> 5);
+        if (sb * T < r1) { const vela_gnstat st = gs[sb * 32 + (i & 31)]; s_p[i >> 5][i & 31] = norm_params(st.mean, st.e, st.sd); }
     }
     __syncthreads();
-    if (r >= M) return;
-    const long long* s_mean = sm_mean[slot]; const long long* s_sd = sm_sd[slot]; const unsigned long long* s_inv = sm_inv[slot]; const int* s_e = sm_e[slot];
-    const int cg = C >> 5, C4 = C >> 2;
-    const int32_t* x = X + size_t(r) * C;
-    u32 m = 0;
-    int v[QUANT ? 4 * R4 : 4];
-    #pragma unroll
-    for (int j = 0; j < (QUANT ? R4 : 64); ++j) {
-        const int c4 = lane + 32 * j;
-        if (c4 >= C4) break;
-        const int c = c4 * 4;
-        const int4 xv = __ldg(reinterpret_cast<const int4*>(x + c)), gv = __ldg(reinterpret_cast<const int4*>(g + c)), bv = __ldg(reinterpret_cast<const int4*>(beta + c));
-        const int xa[4] = {xv.x, xv.y, xv.z, xv.w}, ga[4] = {gv.x, gv.y, gv.z, gv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
-        const int g0 = c / cg, cut = (g0 + 1) * cg;      // groups of >= 4 channels: at most one boundary in a quad
-        int y[4];
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int gi = cg >= 4 ? ((c + k) >= cut ? g0 + 1 : g0) : (c + k) / cg;
-            int val = norm_val(xa[k], s_mean[gi], s_e[gi], s_sd[gi], s_inv[gi], ga[k], ba[k]);
-            if (Lsig) val = lut_act(val, Lsig);
-            y[k] = val; m = max(m, uabs(val));
-        }
-        if constexpr (QUANT) {
+    const int rr = threadIdx.x / PT;
+    int y[QUANT ? GN_RPT : 1][2];
+    if (rr < RP) {
+        for (int pr = threadIdx.x % PT; pr < P2; pr += PT) {
+            const int c = 2 * pr, g0 = c / cg, g1 = (c + 1) / cg;
+            const int2 gv = __ldg(reinterpret_cast<const int2*>(g + c)), bv = __ldg(reinterpret_cast<const int2*>(beta + c));
+            int cur = -1;
+            NormP p0, p1;
             #pragma unroll
-            for (int k = 0; k < 4; ++k) v[4 * j + k] = y[k];
-        } else {
-            *reinterpret_cast<int4*>(Y + size_t(r) * C + c) = make_int4(y[0], y[1], y[2], y[3]);
+            for (int i = 0; i < GN_RPT; ++i) {
+                const int r = r0 + rr + i * RP;
+                if (r >= r1) break;
+                const int sl = r / T - b0;
+                if (sl != cur) { p0 = s_p[sl][g0]; p1 = s_p[sl][g1]; cur = sl; }
+                const int2 xv = __ldg(reinterpret_cast<const int2*>(X + size_t(r) * C + c));
+                int v0 = norm_val(xv.x, p0, gv.x, bv.x), v1 = norm_val(xv.y, p1, gv.y, bv.y);
+                if (Lsig) { v0 = lut_act_smem(v0, s_lut); v1 = lut_act_smem(v1, s_lut); }
+                if constexpr (QUANT) { y[i][0] = v0; y[i][1] = v1; }
+                else *reinterpret_cast<int2*>(Y + size_t(r) * C + c) = make_int2(v0, v1);
+                const u32 m = max(uabs(v0), uabs(v1));
+                if (m) atomicMax(&s_rmax[r - r0], m);
+            }
         }
     }
-    m = warp_umax(m);
-    if constexpr (!QUANT) { if (lane == 0) pm[r] = m; return; }
-    else {
-        const int ee = row_exp(m);
-        int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
-        if (lane == 0) e[r] = ee;
-        #pragma unroll
-        for (int j = 0; j < R4; ++j) {
-            const int c4 = lane + 32 * j;
-            if (c4 >= C4) break;
-            store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+    __syncthreads();
+    if constexpr (!QUANT) {
+        for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) pm[r0 + i] = s_rmax[i];
+    } else {
+        for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) e[r0 + i] = row_exp(s_rmax[i]);
+        if (rr < RP) {
+            const int c = 2 * (threadIdx.x % PT);      // QUANT: C / 2 <= 1024, one pair per thread
+            #pragma unroll
+            for (int i = 0; i < GN_RPT; ++i) {
+                const int r = r0 + rr + i * RP;
+                if (r >= r1) break;
+                const int ee = row_exp(s_rmax[r - r0]);
+                const int q0 = quant16(y[i][0], ee), q1 = quant16(y[i][1], ee);
+                *reinterpret_cast<uint16_t*>(hi + size_t(r) * Kp + c) = uint16_t(((q0 >> 8) & 255) | (((q1 >> 8) & 255) << 8));
+                *reinterpret_cast<uint16_t*>(lo + size_t(r) * Kp + c) = uint16_t((((q0 & 255) - 128) & 255) | ((((q1 & 255) - 128) & 255) << 8));
+            }
         }
-        pad_cols(h, l, C, Kp, lane);
+        const int pad = Kp - C;
+        for (int i = threadIdx.x; i < (r1 - r0) * pad; i += blockDim.x) {
+            const int r = r0 + i / pad, cc = C + i % pad;
+            hi[size_t(r) * Kp + cc] = 0; lo[size_t(r) * Kp + cc] = -128;
+        }
     }
 }
 
 // ---------------------------------------------------------------- LayerNorm (src/kernels.cu:223-284,350-419)
 // one warp per row, the row held in registers (C <= 128 * R4, C % 4 == 0)
+// Per-launch constants of the row statistics: floor((2^64 - 1) / d) for the exact divisions by d = C and d = den.
+struct LnConst { uint64_t inv_n; i64 den; uint64_t inv_den; };
 template <int R4, bool QUANT, typename GT>
-__global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const GT* __restrict__ g, const GT* __restrict__ beta, i64 den,
+__global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const GT* __restrict__ g, const GT* __restrict__ beta, const LnConst k,
                              int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp, int32_t* __restrict__ Y) {
     const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= M) return;
@@ -273,7 +316,7 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
         v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
     }
     sum = warp_sum64(sum); mn = warp_min(mn); mx = warp_max(mx);
-    const i64 n = C, mean = floor_div(sum + n / 2, n);
+    const i64 n = C, mean = floor_div_inv(sum + n / 2, uint64_t(n), k.inv_n);
     const i64 rng = max(i64(mx) - mean, mean - i64(mn));
     const int ex = max(0, (rng >= (i64(1) << 32) ? 17 : row_exp(u32(rng))) - 5);
     i64 ss = 0;
@@ -284,11 +327,11 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
         for (int k = 0; k < 4; ++k) { const i64 d = i64(v[4 * j + k]) - mean; const i64 dd = ex ? ((d >> ex) + ((d >> (ex - 1)) & 1)) : d; ss += dd * dd; }
     }
     ss = warp_sum64(ss);
-    const i64 var = floor_div(ss, n);
-    const int shb = 32 - 2 * ex; const i64 one = shb >= 0 ? (i64(1) << shb) : 0;
-    const i64 eps = floor_div(one + den / 2, den);
+    const i64 var = floor_div_inv(ss, uint64_t(n), k.inv_n);
+    const int shb = 32 - 2 * ex;
+    const i64 eps = floor_div_inv((shb >= 0 ? (i64(1) << shb) : 0) + k.den / 2, uint64_t(k.den), k.inv_den);
     const i64 sd = isqrt((var + eps) << 16);
-    const uint64_t inv = ~0ull / uint64_t(2 * sd);
+    const NormP np = norm_params(mean, ex, sd);
     u32 m = 0;
     #pragma unroll
     for (int j = 0; j < R4; ++j) {
@@ -297,7 +340,7 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
         #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int c = c4 * 4 + k;
-            v[4 * j + k] = norm_val(v[4 * j + k], mean, ex, sd, inv, int(g[c]), int(beta[c]));
+            v[4 * j + k] = norm_val(v[4 * j + k], np, int(g[c]), int(beta[c]));
             m = max(m, uabs(v[4 * j + k]));
         }
         if (!QUANT) *reinterpret_cast<int4*>(Y + size_t(r) * C + c4 * 4) = make_int4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -479,38 +522,45 @@ void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H
     const int Ho = (H - 1) / stride + 1, Wo = (W - 1) / stride + 1, rows = B * Ho * Wo, Mpad = (rows + 31) / 32 * 32;
     im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
 }
-static int gn_rows_per_block(int B, int T) { int chunks = std::max(1, (148 * 4) / std::max(1, B)); return std::max(1, ceil_div(T, chunks)); }
 // statistics: accumulate sum/min/max, then the squared deviations, then mean/e/sd per (sample, group)
 void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs) {
-    VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 32 == 0 && C % 4 == 0 && C <= 4096, "gn_stats: C must be a multiple of 32 (32 groups)");
-    const int cnt = B * 32, rpb = gn_rows_per_block(B, T);
+    VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 32 == 0 && C <= 4096, "gn_stats: C must be a multiple of 32 (32 groups), at most 4096");
+    const int cnt = B * 32, Q = C / 4, RP = std::max(1, 512 / Q);
+    const int chunks = std::max(1, std::min(ceil_div(T, 4 * RP), (sm_count() * 4) / B));
+    const int rpb = ceil_div(T, chunks);
     gn_init_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt);
     const dim3 grid(ceil_div(T, rpb), B);
-    const int threads = std::min(1024, (C / 4 + 31) / 32 * 32);
-    gn_pass1_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
-    gn_pass2_kernel<<<grid, threads, 0, st>>>(X, T, C, rpb, gs);
+    gn_stats_kernel<1><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs);
+    gn_stats_kernel<2><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs);
     gn_finish_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt, i64(T) * (C / 32), den);
 }
 void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
               const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
-    VELA_REQUIRE(X && gs && g && beta && C % 32 == 0, "gn_apply: C must be a multiple of 32 (32 groups)");
-    const int M = B * T; const unsigned blocks = ceil_div(M, 8);
+    VELA_REQUIRE(X && gs && g && beta && C % 32 == 0 && C <= 4096 && B > 0 && T > 0, "gn_apply: C must be a multiple of 32 (32 groups), at most 4096");
+    const int M = B * T, PT = std::min(C / 2, 1024), RP = std::max(1, 512 / PT);
+    // rows per block: RP x GN_RPT (at most 256: row maxima in shared memory), touching at most GN_SPAN samples
+    int rpb = std::min(256, RP * GN_RPT);
+    if (rpb > 2 * T) rpb = std::max(1, 2 * T);
+    const int rp = std::min(RP, rpb);
+    const unsigned blocks = ceil_div(M, rpb);
     if (hi) {
-        VELA_REQUIRE(lo && e && Kp >= C && C <= 1280, "gn_apply: quantised output needs C <= 1280");
-        if (C <= 384) gn_apply_kernel<3, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
-        else if (C <= 640) gn_apply_kernel<5, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
-        else gn_apply_kernel<10, true><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        VELA_REQUIRE(lo && e && Kp >= C && C <= 2048 && Kp % 2 == 0, "gn_apply: quantised output needs lo, e, C <= 2048 and Kp >= C even");
+        gn_apply_kernel<true><<<blocks, PT * rp, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
     } else {
         VELA_REQUIRE(Y && pm, "gn_apply: int32 output needs Y and pm");
-        gn_apply_kernel<1, false><<<blocks, 256, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp);
+        gn_apply_kernel<false><<<blocks, PT * rp, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
     }
 }
 template <bool QUANT, typename GT>
 static void lnorm_dispatch(cudaStream_t st, const int32_t* X, int M, int C, const GT* g, const GT* beta, i64 den, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int32_t* Y) {
+    VELA_REQUIRE(den > 0 && C > 0, "lnorm: den and C must be positive");
+    LnConst k;
+    k.inv_n = ~uint64_t(0) / uint64_t(C);
+    k.den = den; k.inv_den = ~uint64_t(0) / uint64_t(den);
     const unsigned blocks = ceil_div(M, 8);
-    if (C <= 384) lnorm_kernel<3, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
-    else if (C <= 640) lnorm_kernel<5, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
-    else if (C <= 1280) lnorm_kernel<10, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, den, hi, lo, e, Kp, Y);
+    if (C <= 384) lnorm_kernel<3, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, k, hi, lo, e, Kp, Y);
+    else if (C <= 640) lnorm_kernel<5, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, k, hi, lo, e, Kp, Y);
+    else if (C <= 1280) lnorm_kernel<10, QUANT, GT><<<blocks, 256, 0, st>>>(X, M, C, g, beta, k, hi, lo, e, Kp, Y);
     else throw Error(VELA_ERR_ARG, "lnorm: C must be <= 1280");
 }
 void lnorm_q(cudaStream_t st, const int32_t* X, int M, int C, const int32_t* g, const int32_t* beta, i64 den, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
