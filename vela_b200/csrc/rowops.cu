@@ -32,15 +32,6 @@ __device__ __forceinline__ i64 floor_div_inv(i64 a, uint64_t d, uint64_t inv) {
     return r ? -i64(q) - 1 : -i64(q);
 }
 
-// lut_act (intops.cuh) with the table staged in shared memory as (L[i], L[i+1] - L[i])
-__device__ __forceinline__ int lut_act_smem(int x, const int2* __restrict__ L2) {
-    int l;
-    if (x < -(16 << 16)) l = 0;
-    else if (x >= (16 << 16)) l = 65536;
-    else { const int z = x + (16 << 16); const int2 t = L2[z >> 10]; l = t.x + ((t.y * (z & 1023)) >> 10); }
-    return int(rshr_pos(i64(x) * l, 16));
-}
-
 // 16 quantised values of one row written as hi / lo bytes at column c (c % 4 == 0)
 __device__ __forceinline__ void store_q4(int8_t* hi, int8_t* lo, int c, int q0, int q1, int q2, int q3) {
     *reinterpret_cast<u32*>(hi + c) = pack_hi4(q0, q1, q2, q3);
@@ -218,76 +209,87 @@ __device__ __forceinline__ int norm_val(int x, const NormP& p, int g, int beta) 
     else if (r >= p.D) q += 1.0;
     return int(sat32(rshr_pos(i64(q) * g, 16) + beta));
 }
-// Apply.  Block = PT x RP threads over rowsPerBlock consecutive rows, GN_RPT rows per thread: a thread owns a
-// channel pair (int2; pairs cover the row with stride PT = min(C/2, 1024)); the pair's group constants
-// (one group unless C/32 is odd and the pair straddles two) of the samples the block touches (at most GN_SPAN)
-// are staged in shared memory, g / beta stay in registers, the SiLU table is staged as (L[i], L[i+1] - L[i]),
-// and the pixel max of each row is combined with shared-memory atomics.  QUANT (C <= 2048): the rows stay in
-// registers until their maxima give the exponents, then hi / lo planes are written.
+// SiLU: sat32(rshr(x lut16(x), 16)), lut16 from the table staged in shared memory as (L[i], L[i+1] - L[i])
+__device__ __forceinline__ int silu_s(int x, const int2* __restrict__ L2) {
+    int l;
+    if (x < -(16 << 16)) l = 0;
+    else if (x >= (16 << 16)) l = 65536;
+    else { const int z = x + (16 << 16); const int2 t = L2[z >> 10]; l = t.x + ((t.y * (z & 1023)) >> 10); }
+    return int(rshr_pos(i64(x) * l, 16));
+}
+// Apply.  Block = PT x RP threads over rowsPerBlock consecutive rows, GN_RPT rows per thread: a thread owns the
+// channel pairs pr, pr + PT, ... (int2; PT = min(C/2, 512)); the pair's group constants (one group unless C/32
+// is odd and the pair straddles two) of the samples the block touches (at most GN_SPAN) are staged in shared
+// memory, the SiLU table as (L[i], L[i+1] - L[i]); the pixel max of each row is combined with shared-memory
+// atomics.  QUANT: the normalised rows are kept in shared memory (dynamic, rowsPerBlock x C int32) until their
+// maxima give the exponents, then hi / lo planes are written.
 constexpr int GN_RPT = 8, GN_SPAN = 4;
 template <bool QUANT>
-__global__ void __launch_bounds__(1024) gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs,
-                                                        const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
-                                                        int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
-                                                        int32_t* __restrict__ e, int Kp, int rowsPerBlock) {
+__global__ void __launch_bounds__(512) gn_apply_kernel(const int32_t* __restrict__ X, int M, int T, int C, const vela_gnstat* __restrict__ gs,
+                                                       const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
+                                                       int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                                                       int32_t* __restrict__ e, int Kp, int rowsPerBlock) {
     __shared__ int2 s_lut[2048];
     __shared__ NormP s_p[GN_SPAN][32];
     __shared__ u32 s_rmax[256];
-    const int P2 = C >> 1, PT = min(P2, 1024), RP = blockDim.x / PT, cg = C >> 5;
-    const int r0 = blockIdx.x * rowsPerBlock, r1 = min(M, r0 + rowsPerBlock), b0 = r0 / T;
+    extern __shared__ int32_t s_rows[];            // QUANT: [rowsPerBlock][C]
+    const int P2 = C >> 1, PT = min(P2, 512), RP = blockDim.x / PT, cg = C >> 5;
     if (Lsig) for (int i = threadIdx.x; i < 2048; i += blockDim.x) { const int x0 = __ldg(Lsig + i), x1 = __ldg(Lsig + i + 1); s_lut[i] = make_int2(x0, x1 - x0); }
-    for (int i = threadIdx.x; i < rowsPerBlock; i += blockDim.x) s_rmax[i] = 0;
-    for (int i = threadIdx.x; i < GN_SPAN * 32; i += blockDim.x) {
-        const int sb = b0 + (i >> 5);
-        if (sb * T < r1) { const vela_gnstat st = gs[sb * 32 + (i & 31)]; s_p[i >> 5][i & 31] = norm_params(st.mean, st.e, st.sd); }
-    }
-    __syncthreads();
     const int rr = threadIdx.x / PT;
-    int y[QUANT ? GN_RPT : 1][2];
-    if (rr < RP) {
-        for (int pr = threadIdx.x % PT; pr < P2; pr += PT) {
-            const int c = 2 * pr, g0 = c / cg, g1 = (c + 1) / cg;
-            const int2 gv = __ldg(reinterpret_cast<const int2*>(g + c)), bv = __ldg(reinterpret_cast<const int2*>(beta + c));
-            int cur = -1;
-            NormP p0, p1;
-            #pragma unroll
-            for (int i = 0; i < GN_RPT; ++i) {
-                const int r = r0 + rr + i * RP;
-                if (r >= r1) break;
-                const int sl = r / T - b0;
-                if (sl != cur) { p0 = s_p[sl][g0]; p1 = s_p[sl][g1]; cur = sl; }
-                const int2 xv = __ldg(reinterpret_cast<const int2*>(X + size_t(r) * C + c));
-                int v0 = norm_val(xv.x, p0, gv.x, bv.x), v1 = norm_val(xv.y, p1, gv.y, bv.y);
-                if (Lsig) { v0 = lut_act_smem(v0, s_lut); v1 = lut_act_smem(v1, s_lut); }
-                if constexpr (QUANT) { y[i][0] = v0; y[i][1] = v1; }
-                else *reinterpret_cast<int2*>(Y + size_t(r) * C + c) = make_int2(v0, v1);
-                const u32 m = max(uabs(v0), uabs(v1));
-                if (m) atomicMax(&s_rmax[r - r0], m);
-            }
+    // PT % 32 == 0 (C % 64 == 0, every UNet width): a warp's lanes share the row, so its row max is reduced first
+    const bool warp_rows = (PT & 31) == 0;
+    const int nchunks = (M + rowsPerBlock - 1) / rowsPerBlock;
+    // the block walks row chunks (the table above is staged once per block)
+    for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+        const int r0 = chunk * rowsPerBlock, r1 = min(M, r0 + rowsPerBlock), b0 = r0 / T;
+        for (int i = threadIdx.x; i < rowsPerBlock; i += blockDim.x) s_rmax[i] = 0;
+        for (int i = threadIdx.x; i < GN_SPAN * 32; i += blockDim.x) {
+            const int sb = b0 + (i >> 5);
+            if (sb * T < r1) { const vela_gnstat st = gs[sb * 32 + (i & 31)]; s_p[i >> 5][i & 31] = norm_params(st.mean, st.e, st.sd); }
         }
-    }
-    __syncthreads();
-    if constexpr (!QUANT) {
-        for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) pm[r0 + i] = s_rmax[i];
-    } else {
-        for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) e[r0 + i] = row_exp(s_rmax[i]);
+        __syncthreads();
         if (rr < RP) {
-            const int c = 2 * (threadIdx.x % PT);      // QUANT: C / 2 <= 1024, one pair per thread
-            #pragma unroll
-            for (int i = 0; i < GN_RPT; ++i) {
-                const int r = r0 + rr + i * RP;
-                if (r >= r1) break;
-                const int ee = row_exp(s_rmax[r - r0]);
-                const int q0 = quant16(y[i][0], ee), q1 = quant16(y[i][1], ee);
-                *reinterpret_cast<uint16_t*>(hi + size_t(r) * Kp + c) = uint16_t(((q0 >> 8) & 255) | (((q1 >> 8) & 255) << 8));
-                *reinterpret_cast<uint16_t*>(lo + size_t(r) * Kp + c) = uint16_t((((q0 & 255) - 128) & 255) | ((((q1 & 255) - 128) & 255) << 8));
+            for (int pr = threadIdx.x % PT; pr < P2; pr += PT) {
+                const int c = 2 * pr, g0 = c / cg, g1 = (c + 1) / cg;
+                const int2 gv = __ldg(reinterpret_cast<const int2*>(g + c)), bv = __ldg(reinterpret_cast<const int2*>(beta + c));
+                int cur = -1;
+                NormP p0, p1;
+                #pragma unroll 4
+                for (int i = 0; i < GN_RPT; ++i) {
+                    const int r = r0 + rr + i * RP;
+                    if (r >= r1) break;
+                    int sl = 0;                                 // sample slot of row r (the chunk spans at most GN_SPAN)
+                    #pragma unroll
+                    for (int k = 1; k < GN_SPAN; ++k) sl += r >= (b0 + k) * T;
+                    if (sl != cur) { p0 = s_p[sl][g0]; p1 = s_p[sl][g1]; cur = sl; }
+                    const int2 xv = __ldg(reinterpret_cast<const int2*>(X + size_t(r) * C + c));
+                    int v0 = norm_val(xv.x, p0, gv.x, bv.x), v1 = norm_val(xv.y, p1, gv.y, bv.y);
+                    if (Lsig) { v0 = silu_s(v0, s_lut); v1 = silu_s(v1, s_lut); }
+                    if constexpr (QUANT) *reinterpret_cast<int2*>(s_rows + (r - r0) * C + c) = make_int2(v0, v1);
+                    else *reinterpret_cast<int2*>(Y + size_t(r) * C + c) = make_int2(v0, v1);
+                    u32 m = max(uabs(v0), uabs(v1));
+                    if (warp_rows) { m = __reduce_max_sync(0xffffffffu, m); if ((threadIdx.x & 31) == 0 && m) atomicMax(&s_rmax[r - r0], m); }
+                    else if (m) atomicMax(&s_rmax[r - r0], m);
+                }
             }
         }
-        const int pad = Kp - C;
-        for (int i = threadIdx.x; i < (r1 - r0) * pad; i += blockDim.x) {
-            const int r = r0 + i / pad, cc = C + i % pad;
-            hi[size_t(r) * Kp + cc] = 0; lo[size_t(r) * Kp + cc] = -128;
+        __syncthreads();
+        if constexpr (!QUANT) {
+            for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) pm[r0 + i] = s_rmax[i];
+        } else {
+            for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) e[r0 + i] = row_exp(s_rmax[i]);
+            // planes: one thread per 4 columns of a row, value 0 = (hi 0, lo -128) in the padding columns [C, Kp)
+            const int K4 = Kp >> 2;
+            for (int i = threadIdx.x; i < (r1 - r0) * K4; i += blockDim.x) {
+                const int rl = i / K4, c = (i - rl * K4) * 4;
+                const int ee = row_exp(s_rmax[rl]);
+                int q[4];
+                #pragma unroll
+                for (int k = 0; k < 4; ++k) q[k] = c + k < C ? quant16(s_rows[rl * C + c + k], ee) : 0;
+                store_q4(hi + size_t(r0 + rl) * Kp, lo + size_t(r0 + rl) * Kp, c, q[0], q[1], q[2], q[3]);
+            }
         }
+        __syncthreads();      // s_rmax, s_p and s_rows are reused by the next chunk
     }
 }
 
@@ -537,15 +539,17 @@ void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, v
 void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
               const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
     VELA_REQUIRE(X && gs && g && beta && C % 32 == 0 && C <= 4096 && B > 0 && T > 0, "gn_apply: C must be a multiple of 32 (32 groups), at most 4096");
-    const int M = B * T, PT = std::min(C / 2, 1024), RP = std::max(1, 512 / PT);
-    // rows per block: RP x GN_RPT (at most 256: row maxima in shared memory), touching at most GN_SPAN samples
+    const int M = B * T, PT = std::min(C / 2, 512), RP = std::max(1, 512 / PT);
+    // rows per block: RP x GN_RPT (at most 256: row maxima in shared memory), touching at most GN_SPAN samples;
+    // the quantised form also keeps its rows in at most 24 KB of shared memory (48 KB per block in all)
     int rpb = std::min(256, RP * GN_RPT);
+    if (hi) rpb = std::min(rpb, std::max(1, 24576 / (4 * C)));
     if (rpb > 2 * T) rpb = std::max(1, 2 * T);
     const int rp = std::min(RP, rpb);
-    const unsigned blocks = ceil_div(M, rpb);
+    const unsigned blocks = std::min(ceil_div(M, rpb), sm_count() * 4);
     if (hi) {
-        VELA_REQUIRE(lo && e && Kp >= C && C <= 2048 && Kp % 2 == 0, "gn_apply: quantised output needs lo, e, C <= 2048 and Kp >= C even");
-        gn_apply_kernel<true><<<blocks, PT * rp, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
+        VELA_REQUIRE(lo && e && Kp >= C && Kp % 4 == 0 && C <= 6144, "gn_apply: quantised output needs lo, e, C <= 6144 and Kp >= C, Kp % 4 == 0");
+        gn_apply_kernel<true><<<blocks, PT * rp, size_t(rpb) * C * 4, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
     } else {
         VELA_REQUIRE(Y && pm, "gn_apply: int32 output needs Y and pm");
         gn_apply_kernel<false><<<blocks, PT * rp, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
