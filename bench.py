@@ -428,8 +428,24 @@ class LinearCase:
     def report(self):
         M, N, K = self.shape
         ms = _time_ms(self.stream, self.launch)
-        return {"kernel": f"gemm_w8a16 {self.kind} (64x64 level)", "M": M, "N": N, "K": K, "ms": round(ms, 4),
-                "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
+        rep = {"kernel": f"gemm_w8a16 {self.kind} (64x64 level)", "M": M, "N": N, "K": K, "ms": round(ms, 4),
+               "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
+        if self.kind == "linear":
+            # the same product with the input quantised once into planes first (vela_quant_rows) and the planar GEMM
+            import torch
+            from vela_b200 import abi
+            hi = torch.empty((M, K), dtype=torch.int8, device=self.X.device); lo = torch.empty_like(hi)
+            e = torch.empty((M,), dtype=torch.int32, device=self.X.device)
+            a = abi.ASrc(); a.src = abi.SRC_I8; a.hi = hi.data_ptr(); a.lo = lo.data_ptr(); a.ld8 = K; a.e = e.data_ptr()
+            st = self.stream.cuda_stream
+            quant = lambda: self.V.check(self.L.vela_quant_rows(st, self.ptr(self.X.data_ptr()), M, K, K, self.ptr(hi.data_ptr()),
+                                                                self.ptr(lo.data_ptr()), self.ptr(e.data_ptr()), K))
+            gemm = lambda: self.V.check(self.L.vela_gemm_w8a16(st, self.byref(a), M, M, self.ptr(self.W.data_ptr()), K, N, N, K,
+                                                               self.ptr(self.cst.data_ptr()), self.byref(self.E)))
+            quant()
+            rep["planar_quant_ms"] = round(_time_ms(self.stream, quant), 4)
+            rep["planar_gemm_ms"] = round(_time_ms(self.stream, gemm), 4)
+        return rep
 
 
 # ------------------------------------------------------------------ CPU baseline (the oracle, bounded sample)

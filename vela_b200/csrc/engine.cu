@@ -426,9 +426,24 @@ private:
         if (!rm) { uint32_t* p = static_cast<uint32_t*>(arena_.alloc(size_t(rows) * 4)); pixmax(st_, x.d, rows, x.C, p); rm = p; }
         Tensor y; y.B = x.B; y.T = x.T; y.C = L.N; y.d = out ? out : static_cast<int32_t*>(arena_.alloc(y.n() * 4));
         if (wantRowmax) y.rowmax = rowmax_alloc(rows);
-        vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_X32; A.x = x.d; A.ldx = x.C; A.rowmax = rm; A.K = L.K;
-        gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, y.rowmax));
+        gemm_x(x.d, rows, x.C, rm, L, epi_plain(y.d, L.N, residual, y.rowmax));
         return y;
+    }
+    // GEMM on an int32 input with known row maxima.  Large inputs are quantised once into hi / lo planes (one read,
+    // planes in the arena) and run on the planar TMA path, which spares the GEMM the per-column-tile re-quantising
+    // of the quantise-on-load source; small ones quantise on load.
+    void gemm_x(const int32_t* xd, int rows, int K, const uint32_t* rm, const Lin& L, const vela_aepi& E) {
+        if (size_t(rows) * size_t(K) >= (size_t(1) << 21) && K % 4 == 0) {
+            const int Mp = int(align_up(rows, 64));
+            int8_t* hi = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp)); int8_t* lo = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp));
+            int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
+            quant_rows_rm(st_, xd, rm, rows, K, K, hi, lo, e, L.Kp, Mp);
+            vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;
+            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
+            return;
+        }
+        vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_X32; A.x = xd; A.ldx = K; A.rowmax = rm; A.K = L.K;
+        gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
     }
     // 3x3 pad-1 convolution (Engine::conv3, src/engine.cu:254-280): implicit GEMM on the int32 image
     Tensor conv3(const Tensor& x, int H, int W, const Lin& L, int stride, int32_t* out = nullptr, const int32_t* residual = nullptr, const uint32_t* pmIn = nullptr) {
@@ -582,8 +597,8 @@ private:
             vela_aepi E; std::memset(&E, 0, sizeof(E)); E.epi = VELA_EPI_GEGLU; E.Y = v.d; E.ldy = F; E.Lphi = m_.lut_phi; E.rowmax = v.rowmax;
             gemm_w8a16(st_, A, n.Mp, n.rows(), Li.w, Li.Kp, Li.Np, Li.N, Li.Kp, Li.cst, E);
             const Lin& L2 = m_.lin(b + ".ff.net.2");
-            vela_asrc A2; std::memset(&A2, 0, sizeof(A2)); A2.src = VELA_SRC_X32; A2.x = v.d; A2.ldx = F; A2.rowmax = v.rowmax; A2.K = F;
-            gemm_w8a16(st_, A2, int(align_up(B * T, 64)), B * T, L2.w, L2.Kp, L2.Np, L2.N, L2.Kp, L2.cst, epi_plain(h.d, C, h.d, h.rowmax));
+            VELA_REQUIRE(L2.K == F, "ff.net.2: K mismatch");
+            gemm_x(v.d, B * T, F, v.rowmax, L2, epi_plain(h.d, C, h.d, h.rowmax));
             arena_.off = m2;
         }
         lin_x(h, m_.lin(p + ".proj_out"), out.d, x.d);

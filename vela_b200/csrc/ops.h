@@ -12,6 +12,8 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
                 const int32_t* cst, const vela_aepi& E);
 void conv_e(cudaStream_t st, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e);
 void quant_rows(cudaStream_t st, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+// quant_rows with the row maxima given (row_exp(rowmax[r]) = the row's exponent); rows [M, Mpad) zero-valued
+void quant_rows_rm(cudaStream_t st, const int32_t* X, const uint32_t* rowmax, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int Mpad);
 void pixmax(cudaStream_t st, const int32_t* X, int rows, int C, uint32_t* pm);
 void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H, int W, int C, int stride, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
 void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs);
