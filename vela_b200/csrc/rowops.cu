@@ -66,6 +66,27 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ X, int M, int Mpad
     pad_cols(h, l, K, Kp, lane);
 }
 
+// Row quantisation with the row maxima already known (the producing epilogue's row max): one read of X.
+// Block = 256 threads over rows of K / 4 int4 quads each (K % 4 == 0); rows [M, Mpad) become value 0.
+__global__ void quant_rows_rm_kernel(const int32_t* __restrict__ X, const u32* __restrict__ rowmax, int M, int Mpad, int K, int ldx,
+                                     int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
+    const int Q = Kp >> 2;                                 // output quads per row (K quads carry data, the rest is padding)
+    const size_t n = size_t(Mpad) * Q;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+        const int r = int(i / Q), c = int(i - size_t(r) * Q) * 4;
+        int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+        if (r < M) {
+            const int ee = row_exp(__ldg(rowmax + r));
+            if (c == 0) e[r] = ee;
+            if (c < K) {
+                const int4 v = __ldg(reinterpret_cast<const int4*>(X + size_t(r) * ldx + c));
+                q0 = quant16(v.x, ee); q1 = quant16(v.y, ee); q2 = quant16(v.z, ee); q3 = quant16(v.w, ee);
+            }
+        } else if (c == 0) e[r] = 0;
+        store_q4(hi + size_t(r) * Kp, lo + size_t(r) * Kp, c, q0, q1, q2, q3);
+    }
+}
+
 // ---------------------------------------------------------------- pixel max (src/kernels.cu:106-115)
 __global__ void pixmax_kernel(const int32_t* __restrict__ X, int rows, int C, u32* __restrict__ pm) {
     const int lane = threadIdx.x & 31, r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -514,6 +535,12 @@ void quant_rows(cudaStream_t st, const int32_t* X, int M, int K, int ldx, int8_t
     VELA_REQUIRE(X && hi && lo && e && M > 0 && K > 0 && Kp >= K && ldx >= K, "quant_rows: bad arguments");
     const int Mpad = (M + 31) / 32 * 32;
     quant_rows_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, M, Mpad, K, ldx, hi, lo, e, Kp);
+}
+void quant_rows_rm(cudaStream_t st, const int32_t* X, const uint32_t* rowmax, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int Mpad) {
+    VELA_REQUIRE(X && rowmax && hi && lo && e && M > 0 && K > 0 && K % 4 == 0 && ldx % 4 == 0 && Kp >= K && Kp % 4 == 0 && Mpad >= M,
+                 "quant_rows_rm: needs K, ldx and Kp multiples of 4");
+    const size_t n = size_t(Mpad) * (Kp / 4);
+    quant_rows_rm_kernel<<<unsigned(std::min<size_t>((n + 255) / 256, size_t(sm_count()) * 16)), 256, 0, st>>>(X, rowmax, M, Mpad, K, ldx, hi, lo, e, Kp);
 }
 void pixmax(cudaStream_t st, const int32_t* X, int rows, int C, uint32_t* pm) {
     VELA_REQUIRE(X && pm && rows > 0 && C > 0, "pixmax: bad arguments");
