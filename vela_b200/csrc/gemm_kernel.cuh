@@ -57,9 +57,9 @@ __device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ L2) { r
 // (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
 // applies the per-column constants (cst[j] = column n0 + j) and writes the epilogue's outputs.  er is the row's
 // exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory).
-template <int BN, int SRC, int EPI, int NC>
-__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                              int m0, int n0, int rl, int c0, int split, int er) {
+template <int BN, int SRC, int EPI, int NC, bool FAST>
+__device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
+                                                int m0, int n0, int rl, int c0, int split, int er) {
     static_assert(NC % 16 == 0, "16-column chunks");
     const int grow = m0 + rl;
     const bool live = grow < a.Mreal;
@@ -71,7 +71,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
             int hi[16], lo[16];
             tmem_ld16(tl + c0 + c * 16, hi); tmem_ld16(tl + BN + c0 + c * 16, lo); tmem_ld_wait();
             #pragma unroll
-            for (int j = 0; j < 16; ++j) { const int4 cc = cst[c0 + c * 16 + j]; y[c * 16 + j] = epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
+            for (int j = 0; j < 16; ++j) { const int4 cc = cst[c0 + c * 16 + j]; y[c * 16 + j] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
         }
         const int nh = n0 + c0;
         if (live && nh < a.Nreal) {
@@ -142,7 +142,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
             }
             int y[16];
             #pragma unroll
-            for (int j = 0; j < 16; ++j) { const int4 cc = cst[col + j]; y[j] = epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
+            for (int j = 0; j < 16; ++j) {
+                const int4 cc = cst[col + j];
+                y[j] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc));
+            }
             if constexpr (EPI == EPI_PLAIN) {
                 if (a.gelu) {
                     if (L2) {
@@ -158,11 +161,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
                         const int r16[16] = {rv[0].x, rv[0].y, rv[0].z, rv[0].w, rv[1].x, rv[1].y, rv[1].z, rv[1].w,
                                              rv[2].x, rv[2].y, rv[2].z, rv[2].w, rv[3].x, rv[3].y, rv[3].z, rv[3].w};
                         #pragma unroll
-                        for (int j = 0; j < 16; ++j) y[j] = int(sat32(i64(y[j]) + r16[j]));
+                        for (int j = 0; j < 16; ++j) y[j] = add_sat(y[j], r16[j]);
                     } else {
                         const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
                         #pragma unroll
-                        for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) y[j] = int(sat32(i64(y[j]) + __ldg(rp + j)));
+                        for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) y[j] = add_sat(y[j], __ldg(rp + j));
                     }
                 }
                 int32_t* dst = a.Y + size_t(grow) * a.ldy + n;
@@ -194,6 +197,22 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, co
         }
         if (a.rowmax_out && live && mx) atomicMax(a.rowmax_out + grow, mx);
     }
+}
+
+// The shifts s[n] - e[row] of a tile all in [1, 31] (the usual case) take the short epilogue arithmetic; the
+// decision is warp-uniform (srange = the tile's min and max s; the caller votes).
+// (the general arithmetic stays out of line: it is rare and would otherwise raise the register count of the
+// common path)
+template <int BN, int SRC, int EPI, int NC>
+__device__ __noinline__ void gemm_epilogue_general(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
+                                                   int m0, int n0, int rl, int c0, int split, int er) {
+    gemm_epilogue_t<BN, SRC, EPI, NC, false>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
+}
+template <int BN, int SRC, int EPI, int NC>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
+                                              int m0, int n0, int rl, int c0, int split, int er, bool fast) {
+    if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
+    else gemm_epilogue_general<BN, SRC, EPI, NC>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
 }
 
 // Split-K reduction: sum the raw hi/lo partials of every split, then the plain epilogue

@@ -16,6 +16,7 @@
 #pragma once
 #include "gemm_kernel.cuh"
 #include <algorithm>
+#include <climits>
 
 namespace vela {
 
@@ -251,10 +252,15 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             int er = 0;
             if (grow < a.Mreal) er = (SRC == SRC_X32) ? row_exp(__ldg(a.rowmax_in + grow)) : __ldg(a.e + grow);
             asm volatile("bar.sync 2, %0;" :: "r"(Cfg::EW * 32) : "memory");
+            // the tile's range of column shifts s (each lane scans a slice of the staged constants)
+            int smin = INT_MAX, smax = INT_MIN;
+            for (int i = lane; i < BN; i += 32) { const int sv = cb[i].y; smin = min(smin, sv); smax = max(smax, sv); }
+            smin = __reduce_min_sync(0xffffffffu, smin); smax = __reduce_max_sync(0xffffffffu, smax);
+            const bool fast = a.partial == nullptr && __all_sync(0xffffffffu, smin - er >= 1 && smax - er <= 31);
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC));
             if (!ok) continue;
             tc_fence_after();
-            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er);
+            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[b]);

@@ -90,4 +90,16 @@ __device__ __forceinline__ int epi_y(int chi, int clo, int m, int sh, int b, int
     const i64 r = (sh >= 1 && sh <= 62) ? rshr_pos(v, sh) : rshr(v, sh);
     return int(sat32(r + b));
 }
+// saturating int32 addition (sat32 of the exact sum)
+__device__ __forceinline__ int add_sat(int a, int b) { int r; asm("add.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b)); return r; }
+// epi_y for a shift known to lie in [1, 31]: the rounded shift of the 64-bit product is one funnel shift for the
+// low word plus a test that the high word is its sign extension (else the value saturates); + b saturating.
+// (clo + 128 wsum fits 32 bits: |clo|, |128 wsum| <= 128 * 127 * K < 2^30 for K <= 2^16.)
+__device__ __forceinline__ int epi_y_fast(int chi, int clo, int m, int sh, int b, int wsum128) {
+    const i64 v = (i64(chi) * 256 + (clo + wsum128)) * i64(m);
+    const i64 t = v + (i64(1) << (sh - 1));
+    const int lo = int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), sh));
+    const int hs = int(t >> 32) >> sh;
+    return add_sat(hs == (lo >> 31) ? lo : (t < 0 ? INT32_MIN : INT32_MAX), b);
+}
 }  // namespace vela
