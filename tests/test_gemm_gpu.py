@@ -157,6 +157,33 @@ def test_conv_shapes_both_loaders(B, Hh, C, N):
         assert np.array_equal(got, exp), (B, Hh, C, N, stride)
 
 
+@pytest.mark.parametrize("B,Hh,C,N", [(2, 64, 64, 320), (4, 32, 64, 640), (8, 16, 64, 1280)])
+def test_conv_wide_outputs(B, Hh, C, N):
+    """outputs of 2, 4 and 8 column tiles of 160 over many row tiles (the UNet's conv widths)"""
+    rng = np.random.default_rng(N + Hh); d = Dev()
+    X = rbits(rng, (B, Hh, Hh, C), 26)
+    W = rng.integers(-127, 128, (N, 9 * C)).astype(np.int8)
+    c = cst_for(rng, W, N, N)
+    got, exp = conv_case(d, X, W, c, 1)
+    assert np.array_equal(got, exp), (B, Hh, C, N)
+
+
+def test_x32_many_row_tiles():
+    rng = np.random.default_rng(5); d = Dev()
+    M, K, N = 8192, 256, 320
+    X = rbits(rng, (M, K), 28)
+    W = rng.integers(-127, 128, (N, K)).astype(np.int8); c = cst_for(rng, W, N, N)
+    rowmax = np.abs(X.astype(np.int64)).max(1).astype(np.uint32)
+    a = abi.ASrc(); a.src = abi.SRC_X32; a.x = A(d(X)); a.ldx = K; a.K = K; a.rowmax = A(d(rowmax.view(np.int32)))
+    Y = d.empty((M, N), torch.int32, 0x5A)
+    E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = A(Y); E.ldy = N
+    run_gemm(a, M, M, d(W), K, N, N, K, d(c), E)
+    hi, lo, e = O.quant_rows(X, K, M)
+    exp = np.zeros((M, N), np.int32)
+    O.gemm_hl(hi, lo, M, W, N, K, c, e, O.EPI_PLAIN, Y=exp, ldy=N)
+    assert np.array_equal(H(Y), exp)
+
+
 @pytest.mark.parametrize("M,K,N", [(300, 96, 128), (130, 160, 64)])
 def test_x32_ragged_k(M, K, N):
     """int32 source whose K is not a multiple of 64: the staged box past K reads zeros (quantised value 0)"""
