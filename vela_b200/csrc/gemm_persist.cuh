@@ -216,11 +216,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY))) { ok = false; break; }
                 uint32_t hw[8], lw[8];
                 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int q0 = quant16_fast(v[j].x, qs1, qr, qs2), q1 = quant16_fast(v[j].y, qs1, qr, qs2);
-                    const int q2 = quant16_fast(v[j].z, qs1, qr, qs2), q3 = quant16_fast(v[j].w, qs1, qr, qs2);
-                    hw[j] = pack_hi4(q0, q1, q2, q3); lw[j] = pack_lo4(q0, q1, q2, q3);
-                }
+                for (int j = 0; j < 8; ++j) quant_pack4(v[j].x, v[j].y, v[j].z, v[j].w, qs1, qr, qs2, hw[j], lw[j]);
                 uint8_t* st = smem + s * Cfg::STAGE;
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2 + 1)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);

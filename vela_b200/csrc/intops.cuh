@@ -55,6 +55,19 @@ __device__ __forceinline__ int quant16(int v, int e) {
 __device__ __forceinline__ int quant16_fast(int v, int s1, int r, int s2) {
     return min(max(((v >> s1) + r) >> s2, -32767), 32767);
 }
+// Four int32 values quantised with the row's shift split (s1, r, s2) straight into their hi and lo plane bytes:
+// the rounded shift in 32-bit, then pairs narrowed with saturation to 16 bits (cvt.pack.sat: the first source
+// goes to the upper half), -32768 raised to -32767 on both halves at once (max.s16x2), and the byte selections.
+__device__ __forceinline__ void quant_pack4(int v0, int v1, int v2, int v3, int s1, int r, int s2, uint32_t& hw, uint32_t& lw) {
+    const int q0 = ((v0 >> s1) + r) >> s2, q1 = ((v1 >> s1) + r) >> s2, q2 = ((v2 >> s1) + r) >> s2, q3 = ((v3 >> s1) + r) >> s2;
+    uint32_t w01, w23;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w01) : "r"(q1), "r"(q0));
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w23) : "r"(q3), "r"(q2));
+    asm("max.s16x2 %0, %0, %1;" : "+r"(w01) : "r"(0x80018001u));
+    asm("max.s16x2 %0, %0, %1;" : "+r"(w23) : "r"(0x80018001u));
+    hw = __byte_perm(w01, w23, 0x7531);
+    lw = __byte_perm(w01, w23, 0x6420) ^ 0x80808080u;
+}
 // hi bytes / lo bytes of four 16-bit values packed into one word each
 __device__ __forceinline__ u32 pack_hi4(int q0, int q1, int q2, int q3) {
     return __byte_perm(__byte_perm(q0, q1, 0x0051), __byte_perm(q2, q3, 0x0051), 0x5410);
