@@ -169,6 +169,11 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
     a.kb_per_split = ceil_div(a.nkb, pl.splits);
     const int splits = ceil_div(a.nkb, a.kb_per_split);
     if (splits > 1) a.partial = static_cast<int32_t*>(E.workspace);
+    // plain epilogue without split-K: Y leaves through per-warp shared-memory boxes and TMA stores
+    if (epi == EPI_PLAIN && splits == 1 && E.Y && (E.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(E.Y) & 15) == 0) {
+        a.tmY = tmap2d(E.Y, CU_TENSOR_MAP_DATA_TYPE_INT32, uint64_t(Nreal), uint64_t(Mreal), uint64_t(E.ldy) * 4, 16, 32, Swz::B64);
+        a.ytma = 1;
+    }
 
     if (epi == EPI_PLAIN) {
         if (src == VELA_SRC_I8) { if (BN == 128) launch_gemm_persist<128, 6, SRC_I8, EPI_PLAIN>(a, st); else launch_gemm_persist<64, 6, SRC_I8, EPI_PLAIN>(a, st); }

@@ -38,6 +38,8 @@ struct GemmArgs {
     int8_t *qhi, *qlo, *khi, *klo; int32_t *qe, *ke; int64_t *qhs, *qls, *qts, *khs, *kls, *kts;
     int32_t* partial;                                       // split-K: raw s32 [split][2][Mp][Np]
     int rvec;                                               // residual rows 16-byte aligned (int4 loads)
+    CUtensorMap tmY;                                        // plain epilogue with ytma = 1: Y [Mreal][Nreal] int32, box 16 x 32, 64B swizzle
+    int ytma;
     unsigned* err;
 };
 
@@ -59,7 +61,7 @@ __device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ L2) { r
 // exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory).
 template <int BN, int SRC, int EPI, int NC, bool FAST>
 __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                int m0, int n0, int rl, int c0, int split, int er) {
+                                                int m0, int n0, int rl, int c0, int split, int er, uint8_t* yb) {
     static_assert(NC % 16 == 0, "16-column chunks");
     const int grow = m0 + rl;
     const bool live = grow < a.Mreal;
@@ -116,7 +118,8 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
         #pragma unroll 1
         for (int c = 0; c < NC / 16; ++c) {
             const int col = c0 + c * 16, n = n0 + col;
-            const bool act = live && n < a.Nreal;
+            if (n >= a.Nreal) break;                  // warp-uniform: the rest of the slice lies past N
+            const bool act = live;
             const bool full16 = n + 16 <= a.Nreal;
             // residual of this chunk in flight while the accumulators are read (int4 when rows are 16-byte aligned)
             int4 rv[4];
@@ -129,7 +132,9 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             }
             int hi[16], lo[16];
             tmem_ld16(tl + col, hi); tmem_ld16(tl + BN + col, lo); tmem_ld_wait();
-            if (!act) continue;
+            // a TMA-stored plain chunk is written by the whole warp (rows past Mreal are clipped by the store)
+            const bool tstore = EPI == EPI_PLAIN && yb != nullptr;
+            if (!act && !tstore) continue;
             if (a.partial) {             // split-K: raw accumulators, reduced by gemm_splitk_reduce
                 int32_t* ph = a.partial + (size_t(split) * 2 * a.Mp + grow) * a.Np + n;
                 int32_t* pl = ph + size_t(a.Mp) * a.Np;
@@ -140,59 +145,79 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                 }
                 continue;
             }
-            int y[16];
-            #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int4 cc = cst[col + j];
-                y[j] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc));
-            }
             if constexpr (EPI == EPI_PLAIN) {
-                if (a.gelu) {
-                    if (L2) {
-                        #pragma unroll
-                        for (int j = 0; j < 16; ++j) y[j] = lut_act_s(y[j], L2);
-                    } else {
-                        #pragma unroll
-                        for (int j = 0; j < 16; ++j) y[j] = lut_act(y[j], a.Lphi);
-                    }
+                // four columns at a time: y, GELU, + residual, then out (shared-memory box or global) and the row max
+                const int lane = rl & 31;
+                if (tstore) {                            // the previous TMA store has finished reading the box
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
                 }
-                if (a.R) {
-                    if (a.rvec && full16) {
-                        const int r16[16] = {rv[0].x, rv[0].y, rv[0].z, rv[0].w, rv[1].x, rv[1].y, rv[1].z, rv[1].w,
-                                             rv[2].x, rv[2].y, rv[2].z, rv[2].w, rv[3].x, rv[3].y, rv[3].z, rv[3].w};
-                        #pragma unroll
-                        for (int j = 0; j < 16; ++j) y[j] = add_sat(y[j], r16[j]);
-                    } else {
-                        const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
-                        #pragma unroll
-                        for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) y[j] = add_sat(y[j], __ldg(rp + j));
-                    }
-                }
+                const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
                 int32_t* dst = a.Y + size_t(grow) * a.ldy + n;
-                if (full16 && (a.ldy & 3) == 0) {
+                #pragma unroll
+                for (int g4 = 0; g4 < 4; ++g4) {
+                    int y4[4];
+                    #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = 4 * g4 + u;
+                        const int4 cc = cst[col + j];
+                        y4[u] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc));
+                    }
+                    if (a.gelu) {
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) y4[u] = L2 ? lut_act_s(y4[u], L2) : lut_act(y4[u], a.Lphi);
+                    }
+                    if (a.R && act) {
+                        if (a.rvec && full16) {
+                            y4[0] = add_sat(y4[0], rv[g4].x); y4[1] = add_sat(y4[1], rv[g4].y);
+                            y4[2] = add_sat(y4[2], rv[g4].z); y4[3] = add_sat(y4[3], rv[g4].w);
+                        } else {
+                            #pragma unroll
+                            for (int u = 0; u < 4; ++u) if (full16 || n + 4 * g4 + u < a.Nreal) y4[u] = add_sat(y4[u], __ldg(rp + 4 * g4 + u));
+                        }
+                    }
+                    if (tstore) {
+                        *reinterpret_cast<int4*>(yb + sw64_off(lane, g4)) = make_int4(y4[0], y4[1], y4[2], y4[3]);
+                    } else if (full16 && (a.ldy & 3) == 0) {
+                        *reinterpret_cast<int4*>(dst + 4 * g4) = make_int4(y4[0], y4[1], y4[2], y4[3]);
+                    } else {
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) if (n + 4 * g4 + u < a.Nreal) dst[4 * g4 + u] = y4[u];
+                    }
+                    if (act) {
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) if (full16 || n + 4 * g4 + u < a.Nreal) mx = max(mx, uabs(y4[u]));
+                    }
+                }
+                if (tstore) {                            // the warp's 32 rows x 16 columns: one TMA store (rows past Mreal clipped)
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) { tma_store_2d(&a.tmY, yb, n, m0 + (rl & ~31)); bulk_commit(); }
+                }
+            } else {
+                int y[16];
+                #pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int4 cc = cst[col + j];
+                    y[j] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc));
+                }
+                if constexpr (EPI == EPI_GEGLU) {      // interleaved columns 2c = a_c, 2c+1 = g_c
+                    int v[8];
+                    #pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int ge = L2 ? lut_act_s(y[2 * j + 1], L2) : lut_act(y[2 * j + 1], a.Lphi);
+                        v[j] = int(rshr_pos(i64(y[2 * j]) * ge, 16));
+                        mx = max(mx, uabs(v[j]));
+                    }
+                    int32_t* dst = a.Y + size_t(grow) * a.ldy + (n >> 1);
+                    *reinterpret_cast<int4*>(dst) = make_int4(v[0], v[1], v[2], v[3]);
+                    *reinterpret_cast<int4*>(dst + 4) = make_int4(v[4], v[5], v[6], v[7]);
+                } else if constexpr (EPI == EPI_SPLIT3) {
+                    const int part = n >= 2 * a.Cs ? 2 : (n >= a.Cs ? 1 : 0);
+                    int32_t* dst = (part == 0 ? a.Y : (part == 1 ? a.Y1 : a.Y2)) + size_t(grow) * a.Cs + (n - part * a.Cs);
                     #pragma unroll
                     for (int j = 0; j < 16; j += 4) *reinterpret_cast<int4*>(dst + j) = make_int4(y[j], y[j + 1], y[j + 2], y[j + 3]);
-                } else {
-                    for (int j = 0; j < 16; ++j) if (n + j < a.Nreal) dst[j] = y[j];
                 }
-                #pragma unroll
-                for (int j = 0; j < 16; ++j) if (full16 || n + j < a.Nreal) mx = max(mx, uabs(y[j]));
-            } else if constexpr (EPI == EPI_GEGLU) {      // interleaved columns 2c = a_c, 2c+1 = g_c
-                int v[8];
-                #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int ge = L2 ? lut_act_s(y[2 * j + 1], L2) : lut_act(y[2 * j + 1], a.Lphi);
-                    v[j] = int(rshr_pos(i64(y[2 * j]) * ge, 16));
-                    mx = max(mx, uabs(v[j]));
-                }
-                int32_t* dst = a.Y + size_t(grow) * a.ldy + (n >> 1);
-                *reinterpret_cast<int4*>(dst) = make_int4(v[0], v[1], v[2], v[3]);
-                *reinterpret_cast<int4*>(dst + 4) = make_int4(v[4], v[5], v[6], v[7]);
-            } else if constexpr (EPI == EPI_SPLIT3) {
-                const int part = n >= 2 * a.Cs ? 2 : (n >= a.Cs ? 1 : 0);
-                int32_t* dst = (part == 0 ? a.Y : (part == 1 ? a.Y1 : a.Y2)) + size_t(grow) * a.Cs + (n - part * a.Cs);
-                #pragma unroll
-                for (int j = 0; j < 16; j += 4) *reinterpret_cast<int4*>(dst + j) = make_int4(y[j], y[j + 1], y[j + 2], y[j + 3]);
             }
         }
         if (a.rowmax_out && live && mx) atomicMax(a.rowmax_out + grow, mx);
@@ -205,14 +230,14 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
 // common path)
 template <int BN, int SRC, int EPI, int NC>
 __device__ __noinline__ void gemm_epilogue_general(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                   int m0, int n0, int rl, int c0, int split, int er) {
-    gemm_epilogue_t<BN, SRC, EPI, NC, false>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
+                                                   int m0, int n0, int rl, int c0, int split, int er, uint8_t* yb) {
+    gemm_epilogue_t<BN, SRC, EPI, NC, false>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }
 template <int BN, int SRC, int EPI, int NC>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                              int m0, int n0, int rl, int c0, int split, int er, bool fast) {
-    if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
-    else gemm_epilogue_general<BN, SRC, EPI, NC>(a, tl, cst, L2, m0, n0, rl, c0, split, er);
+                                              int m0, int n0, int rl, int c0, int split, int er, bool fast, uint8_t* yb) {
+    if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
+    else gemm_epilogue_general<BN, SRC, EPI, NC>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }
 
 // Split-K reduction: sum the raw hi/lo partials of every split, then the plain epilogue

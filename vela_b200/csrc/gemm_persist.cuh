@@ -7,11 +7,13 @@
 // short-K GEMMs of the UNet (K = 320..1280, 5-20 k-blocks per tile) no longer pay a pipeline fill, a TMEM
 // allocation and an exposed epilogue per tile.
 //
-// Warp roles (THREADS = 32 x (2 + NCW + 8)):
-//   warp 0            TMA producer: W (and A-hi / A-lo planes, or the raw int32 operand into the staging ring)
+// Warp roles (THREADS = 32 x (2 + NCW + EW + XW)):
+//   warp 0            TMA producer: W (and the A-hi / A-lo planes of int8 sources)
 //   warp 1            TMEM allocator and MMA issuer (one elected lane)
 //   warps 2 .. 1+NCW  int32 sources only (NCW = 8): quantise the staged rows into the swizzled A tiles
-//   last 8 warps      epilogue: warp % 4 selects the TMEM lane quarter, the two warps of a quarter split the columns
+//   next 8 or 16      epilogue: warp % 4 selects the TMEM lane quarter, the warps of a quarter split the columns
+//   last warp         int32 sources only: TMA of the raw operand into the staging ring, decoupled from the W ring so
+//                     the staging runs X_STAGES k-blocks ahead of the converters whatever the MMA progress
 // Every wait is bounded; on a timeout the error word is set and each role stops issuing work.
 #pragma once
 #include "gemm_kernel.cuh"
@@ -35,13 +37,18 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static constexpr int EW = (REG || EPI == EPI_QKV) ? 8 : 16;
     static constexpr int NCOL = BN / (EW / 4);                 // columns of a tile per epilogue thread
     static constexpr int EPI_WARP0 = 2 + NCW;
-    static constexpr int THREADS = 32 * (2 + NCW + EW);
+    static constexpr int XW = REG ? 1 : 0;                      // int32 sources: one more warp issues the staging TMA
+    static constexpr int X_WARP = EPI_WARP0 + EW;
+    static constexpr int THREADS = 32 * (2 + NCW + EW + XW);
     static constexpr int CTRL = 1024;
     static constexpr bool SLUT = !REG;                          // GELU table staged in shared memory
     static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [2][BN] column constants (double-buffered by tile)
     static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[2048]
+    // plain epilogue: one 32 x 16 int32 box (2 KB, 64-byte swizzle) per epilogue warp for the TMA store of Y
+    static constexpr int YB_BYTES = EPI == EPI_PLAIN ? EW * 2048 : 0;
+    static constexpr int OFF_YB = (OFF_LUT + (SLUT ? 2048 * 8 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
-    static constexpr int OFF_X = (OFF_LUT + (SLUT ? 2048 * 8 : 0) + 1023) / 1024 * 1024;
+    static constexpr int OFF_X = OFF_YB + YB_BYTES;
     static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
     static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
     static constexpr int SMEM = 1024 + OFF_X + (X_STAGES > 0 ? X_STAGES : 0) * X_STAGE;
@@ -49,6 +56,7 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static_assert(NCOL % 16 == 0 && (EPI != EPI_QKV || NCOL == 64), "epilogue column split");
     static_assert(STAGE % 1024 == 0, "stage alignment");
     static_assert(!REG || X_STAGES >= 2, "int32 sources need a staging ring of at least two stages");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 template <int BN, int STAGES, int SRC, int EPI>
@@ -101,28 +109,8 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM, n0 = (r % nN) * BN;
                 const int kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
-                int cb = 0, cy0 = 0;
-                if (SRC == SRC_CONV32 && a.xtma) { cb = m0 / a.conv_rows_per_img; cy0 = (m0 - cb * a.conv_rows_per_img) / a.Wo; }
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int k = (kb0 + i) * Cfg::BK;
-                    if constexpr (REG) {
-                        if (a.xtma) {
-                            const int xs = g % Cfg::X_STAGES;
-                            if (!mbar_wait(&xempty[xs], ((g / Cfg::X_STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
-                            mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
-                            #pragma unroll
-                            for (int hf = 0; hf < 2; ++hf) {
-                                uint8_t* dst = xstage + xs * Cfg::X_STAGE + hf * Cfg::X_HALF;
-                                const int kk = k + hf * 32;
-                                if (SRC == SRC_X32) tma_load_2d(dst, &a.tmX, &xfull[xs], kk, m0);
-                                else {
-                                    const int tap = kk / a.C, c0 = kk - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
-                                    const int yy = tap < 9 ? cy0 * a.stride + ky - 1 : a.H + 8;   // K padding: a box below the image
-                                    tma_load_4d(dst, &a.tmX, &xfull[xs], tap < 9 ? c0 : 0, kx - 1, yy, cb);
-                                }
-                            }
-                        }
-                    }
                     const int s = g % STAGES;
                     if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
                     uint8_t* st = smem + s * Cfg::STAGE;
@@ -163,9 +151,39 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 mma_commit(&accf[b]);     // fires when every MMA of this tile has completed
             }
         }
+    } else if (REG && warp == Cfg::X_WARP) {
+        // ------------------------------------------------------------ int32 staging TMA (runs ahead of the W ring)
+        if (lane == 0 && a.xtma) {
+            int g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM;
+                const int kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
+                int cb = 0, cy0 = 0;
+                if (SRC == SRC_CONV32) { cb = m0 / a.conv_rows_per_img; cy0 = (m0 - cb * a.conv_rows_per_img) / a.Wo; }
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int k = (kb0 + i) * Cfg::BK;
+                    const int xs = g % Cfg::X_STAGES;
+                    if (!mbar_wait(&xempty[xs], ((g / Cfg::X_STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
+                    #pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        uint8_t* dst = xstage + xs * Cfg::X_STAGE + hf * Cfg::X_HALF;
+                        const int kk = k + hf * 32;
+                        if (SRC == SRC_X32) tma_load_2d(dst, &a.tmX, &xfull[xs], kk, m0);
+                        else {
+                            const int tap = kk / a.C, c0 = kk - tap * a.C, ky = tap / 3, kx = tap - ky * 3;
+                            const int yy = tap < 9 ? cy0 * a.stride + ky - 1 : a.H + 8;   // K padding: a box below the image
+                            tma_load_4d(dst, &a.tmX, &xfull[xs], tap < 9 ? c0 : 0, kx - 1, yy, cb);
+                        }
+                    }
+                }
+            }
+        }
     } else if (REG && warp < Cfg::EPI_WARP0) {
         // ------------------------------------------------------------ A producers (int32 sources)
         const int ct = threadIdx.x - 64;                  // 0..255: row = ct & 127, K half = ct >> 7
+        volatile uint32_t* xsink = reinterpret_cast<uint32_t*>(smem + STAGES * Cfg::STAGE + 512) + warp;
         const int row = ct & 127, half = ct >> 7;
         int g = 0;
         bool ok = true;
@@ -183,16 +201,16 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             }
             // quant16(v, e) = clamp(((v >> (e-1)) + 1) >> 1) for e >= 1, clamp(v) for e = 0
             const int qs1 = er > 0 ? er - 1 : 0, qr = er > 0 ? 1 : 0, qs2 = er > 0 ? 1 : 0;
+            const int qh = (1 << er) >> 1;
+            const bool e15 = __all_sync(0xffffffffu, er <= 15);      // every row of the warp: the two-operation rounding
             for (int i = 0; i < nk; ++i, ++g) {
                 int4 v[8];
+                const int xs = g % Cfg::X_STAGES;
                 if (a.xtma) {
-                    const int xs = g % Cfg::X_STAGES;
                     if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::X_STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL))) { ok = false; break; }
                     const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
                     #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&xempty[xs]);
                 } else {
                     const int k = (kb0 + i) * Cfg::BK + half * 32;
                     const int32_t* src = nullptr;
@@ -212,11 +230,24 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                         for (int j = 0; j < 8; ++j) v[j] = make_int4(0, 0, 0, 0);
                     }
                 }
+                uint32_t hw[8], lw[8];
+                if (e15) {
+                    #pragma unroll
+                    for (int j = 0; j < 8; ++j) quant_pack4_e15(v[j].x, v[j].y, v[j].z, v[j].w, qh, er, hw[j], lw[j]);
+                } else {
+                    #pragma unroll
+                    for (int j = 0; j < 8; ++j) quant_pack4(v[j].x, v[j].y, v[j].z, v[j].w, qs1, qr, qs2, hw[j], lw[j]);
+                }
+                if (a.xtma) {
+                    // release the staging slot: a shared-memory store that needs a value of every staged load (hw[j]
+                    // depends on load j) precedes the arrive, so no read of the slot is in flight when the TMA refills it
+                    if (lane == 0) {
+                        *xsink = hw[0] | hw[1] | hw[2] | hw[3] | hw[4] | hw[5] | hw[6] | hw[7];
+                        mbar_arrive(&xempty[xs]);
+                    }
+                }
                 const int s = g % STAGES;
                 if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY))) { ok = false; break; }
-                uint32_t hw[8], lw[8];
-                #pragma unroll
-                for (int j = 0; j < 8; ++j) quant_pack4(v[j].x, v[j].y, v[j].z, v[j].w, qs1, qr, qs2, hw[j], lw[j]);
                 uint8_t* st = smem + s * Cfg::STAGE;
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2 + 1)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
@@ -227,13 +258,14 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 if (lane == 0) mbar_arrive(&full[s]);
             }
         }
-    } else {
+    } else if (warp < Cfg::EPI_WARP0 + Cfg::EW) {
         // ------------------------------------------------------------ epilogue
         const int ew = warp - Cfg::EPI_WARP0;            // 0 .. EW-1
         const int et = threadIdx.x - Cfg::EPI_WARP0 * 32;
         const int q = warp & 3, hq = ew >> 2;            // TMEM lane quarter (fixed by warp % 4), column slice
         const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
         const int2* lut = (Cfg::SLUT && a.Lphi) ? s_lut : nullptr;
+        uint8_t* yb = (Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 : nullptr;
         bool ok = true;
         int tl = 0;
         // Every epilogue warp runs every tile and every named barrier, also after a timed-out wait (it then skips
@@ -249,18 +281,21 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             if (grow < a.Mreal) er = (SRC == SRC_X32) ? row_exp(__ldg(a.rowmax_in + grow)) : __ldg(a.e + grow);
             asm volatile("bar.sync 2, %0;" :: "r"(Cfg::EW * 32) : "memory");
             // the tile's range of column shifts s (each lane scans a slice of the staged constants)
+            // and of |m| (the short arithmetic forms 256 m in 32 bits)
             int smin = INT_MAX, smax = INT_MIN;
-            for (int i = lane; i < BN; i += 32) { const int sv = cb[i].y; smin = min(smin, sv); smax = max(smax, sv); }
+            u32 mbig = 0;
+            for (int i = lane; i < BN; i += 32) { const int4 cv = cb[i]; smin = min(smin, cv.y); smax = max(smax, cv.y); mbig |= uabs(cv.x) >> 23; }
             smin = __reduce_min_sync(0xffffffffu, smin); smax = __reduce_max_sync(0xffffffffu, smax);
-            const bool fast = a.partial == nullptr && __all_sync(0xffffffffu, smin - er >= 1 && smax - er <= 31);
+            const bool fast = a.partial == nullptr && __all_sync(0xffffffffu, smin - er >= 1 && smax - er <= 31 && mbig == 0);
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC));
             if (!ok) continue;
             tc_fence_after();
-            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast);
+            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast, yb);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[b]);
         }
+        if (yb && lane == 0) bulk_wait0();        // every TMA store of Y has completed before the CTA exits
     }
     tc_fence_before();
     __syncthreads();

@@ -50,6 +50,8 @@ __device__ __forceinline__ int quant16(int v, int e) {
     const int q = e ? (v >> e) + ((v >> (e - 1)) & 1) : v;
     return min(max(q, -32767), 32767);
 }
+// saturating int32 addition (sat32 of the exact sum)
+__device__ __forceinline__ int add_sat(int a, int b) { int r; asm("add.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b)); return r; }
 // quant16 with the row's shift split as (s1, r, s2) = (e - 1, 1, 1) for e >= 1 and (0, 0, 0) for e = 0:
 // ((v >> s1) + r) >> s2 = floor((v + 2^(e-1)) / 2^e) without overflow, then the +-32767 clamp.
 __device__ __forceinline__ int quant16_fast(int v, int s1, int r, int s2) {
@@ -60,6 +62,18 @@ __device__ __forceinline__ int quant16_fast(int v, int s1, int r, int s2) {
 // goes to the upper half), -32768 raised to -32767 on both halves at once (max.s16x2), and the byte selections.
 __device__ __forceinline__ void quant_pack4(int v0, int v1, int v2, int v3, int s1, int r, int s2, uint32_t& hw, uint32_t& lw) {
     const int q0 = ((v0 >> s1) + r) >> s2, q1 = ((v1 >> s1) + r) >> s2, q2 = ((v2 >> s1) + r) >> s2, q3 = ((v3 >> s1) + r) >> s2;
+    uint32_t w01, w23;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w01) : "r"(q1), "r"(q0));
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w23) : "r"(q3), "r"(q2));
+    asm("max.s16x2 %0, %0, %1;" : "+r"(w01) : "r"(0x80018001u));
+    asm("max.s16x2 %0, %0, %1;" : "+r"(w23) : "r"(0x80018001u));
+    hw = __byte_perm(w01, w23, 0x7531);
+    lw = __byte_perm(w01, w23, 0x6420) ^ 0x80808080u;
+}
+// The same for a row exponent e <= 15 (h = 2^e >> 1): every |v| < 2^(15+e) <= 2^30, so v + h cannot overflow and
+// floor((v + 2^(e-1)) / 2^e) is one add and one arithmetic shift.
+__device__ __forceinline__ void quant_pack4_e15(int v0, int v1, int v2, int v3, int h, int e, uint32_t& hw, uint32_t& lw) {
+    const int q0 = (v0 + h) >> e, q1 = (v1 + h) >> e, q2 = (v2 + h) >> e, q3 = (v3 + h) >> e;
     uint32_t w01, w23;
     asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w01) : "r"(q1), "r"(q0));
     asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w23) : "r"(q3), "r"(q2));
@@ -103,14 +117,13 @@ __device__ __forceinline__ int epi_y(int chi, int clo, int m, int sh, int b, int
     const i64 r = (sh >= 1 && sh <= 62) ? rshr_pos(v, sh) : rshr(v, sh);
     return int(sat32(r + b));
 }
-// saturating int32 addition (sat32 of the exact sum)
-__device__ __forceinline__ int add_sat(int a, int b) { int r; asm("add.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b)); return r; }
-// epi_y for a shift known to lie in [1, 31]: the rounded shift of the 64-bit product is one funnel shift for the
+// epi_y for a shift known to lie in [1, 31] and |m| < 2^23: the rounded shift of the 64-bit product is one funnel shift for the
 // low word plus a test that the high word is its sign extension (else the value saturates); + b saturating.
 // (clo + 128 wsum fits 32 bits: |clo|, |128 wsum| <= 128 * 127 * K < 2^30 for K <= 2^16.)
+// The product is formed as two 32x32 -> 64-bit multiply-adds, chi * (256 m) + ((clo + 128 wsum) m + 2^(sh-1)), which
+// needs |m| < 2^23 (the caller checks it per tile).
 __device__ __forceinline__ int epi_y_fast(int chi, int clo, int m, int sh, int b, int wsum128) {
-    const i64 v = (i64(chi) * 256 + (clo + wsum128)) * i64(m);
-    const i64 t = v + (i64(1) << (sh - 1));
+    const i64 t = i64(chi) * (m << 8) + (i64(clo + wsum128) * m + i64(1u << (sh - 1)));
     const int lo = int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), sh));
     const int hs = int(t >> 32) >> sh;
     return add_sat(hs == (lo >> 31) ? lo : (t < 0 ? INT32_MIN : INT32_MAX), b);
