@@ -93,7 +93,8 @@ __device__ __forceinline__ int lut_exp(uint32_t z, const int2* L2) {
 template <int PASS>
 __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ wk, int shq, int r0, int cq, bool fast, bool unif, int eku,
                                              bool full, int kbase, int q, int Tk, int causal, const int2* __restrict__ L2,
-                                             int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l) {
+                                             int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l,
+                                             uint64_t* rel_qk, uint64_t* rel_k) {
     // X and LL first, folded into T (16 registers), then HH: the three accumulators are never all live at once
     int s[16];
     {
@@ -137,6 +138,11 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
             for (int u = 0; u < 16; ++u) s[u] = int(rshr((i64(hh[u]) << 16) + s[u], shq - wk[u]));
         }
     }
+    // every accumulator of the tile is in registers: hand the QK buffer and the K stage back now, so the next
+    // tile's QK products run on the tensor core while this tile's E / P arithmetic runs here
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) { mbar_arrive(rel_qk); mbar_arrive(rel_k); }
     uint32_t vmask = 0xFFFFu;   // validity by key position (a valid score may itself saturate to INT_MIN)
     if (!full) {
         vmask = 0;
@@ -331,13 +337,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                     const uint32_t taddr = tmem + tl + uint32_t(b * 192 + kq * 16);
                     uint32_t pw_h[4], pw_l[4];                        // P bytes of this thread's 16 keys (pass 2)
                     const bool unif = emin == emax;
-                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
-                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
-                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l);
-                    // this warp is done with the QK buffer, the K stage's per-key data and its key staging
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) { mbar_arrive(&qk_free[b]); mbar_arrive(&k_empty[ks]); }
+                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
+                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
+                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
                     if (pass == 2) {
                         ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
                         if (ok) {
