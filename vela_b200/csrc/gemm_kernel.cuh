@@ -45,15 +45,19 @@ struct GemmArgs {
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }
 
-// lut16 / lut_act (intops.cuh) from a table staged in shared memory as (L[i], L[i+1] - L[i]), i < 2048
-__device__ __forceinline__ int lut16_s(int x, const int2* __restrict__ L2) {
-    if (x < -(16 << 16)) return 0;
-    if (x >= (16 << 16)) return 65536;
-    const int z = x + (16 << 16);
-    const int2 e = L2[z >> 10];
-    return e.x + ((e.y * (z & 1023)) >> 10);
+// lut16 / lut_act (intops.cuh) from the table staged in shared memory with sentinels: T[0] = (0, 0) for x below
+// the range, T[1 + i] = (L[i], L[i+1] - L[i]) for i < 2048, T[2049] = (65536, 0) above it, so the range tests
+// become one clamp of the index ((x >> 10) + 1024 = (x + 2^20) >> 10 without the overflow of the sum).
+// Staged only when every L[i] lies in [0, 65536]: then x * lut(x) / 2^16 never exceeds |x| and needs no saturation.
+constexpr int LUT_S_ENTRIES = 2050;
+__device__ __forceinline__ int lut16_s(int x, const int2* __restrict__ T) {
+    const int2 e = T[min(max((x >> 10) + 1024, -1), 2048) + 1];
+    return e.x + ((e.y * (x & 1023)) >> 10);
 }
-__device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ L2) { return int(rshr_pos(i64(x) * lut16_s(x, L2), 16)); }
+__device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ T) {
+    const i64 t = i64(x) * lut16_s(x, T) + 32768;
+    return int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), 16));
+}
 
 // Epilogue of one 128 x BN tile for one thread = one output row (rl) and the NC columns [c0, c0 + NC) of the tile
 // (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
@@ -206,7 +210,10 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                     #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         const int ge = L2 ? lut_act_s(y[2 * j + 1], L2) : lut_act(y[2 * j + 1], a.Lphi);
-                        v[j] = int(rshr_pos(i64(y[2 * j]) * ge, 16));
+                        // sat32(rshr(a * ge, 16)): the funnel shift gives the low word, the high word decides saturation
+                        const i64 t = i64(y[2 * j]) * ge + 32768;
+                        const int lo = int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), 16));
+                        v[j] = (int(t >> 32) >> 16) == (lo >> 31) ? lo : (t < 0 ? INT_MIN : INT_MAX);
                         mx = max(mx, uabs(v[j]));
                     }
                     int32_t* dst = a.Y + size_t(grow) * a.ldy + (n >> 1);

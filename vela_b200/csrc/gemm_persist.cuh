@@ -43,14 +43,15 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static constexpr int CTRL = 1024;
     static constexpr bool SLUT = !REG;                          // GELU table staged in shared memory
     static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [2][BN] column constants (double-buffered by tile)
-    static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[2048]
+    static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[LUT_S_ENTRIES]
     // plain epilogue: one 32 x 16 int32 box (2 KB, 64-byte swizzle) per epilogue warp for the TMA store of Y
     static constexpr int YB_BYTES = EPI == EPI_PLAIN ? EW * 2048 : 0;
-    static constexpr int OFF_YB = (OFF_LUT + (SLUT ? 2048 * 8 : 0) + 1023) / 1024 * 1024;
+    static constexpr int OFF_YB = (OFF_LUT + (SLUT ? LUT_S_ENTRIES * 8 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
     static constexpr int OFF_X = OFF_YB + YB_BYTES;
     static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
     static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
+    static constexpr int XR = X_STAGES > 0 ? X_STAGES : 1;     // ring modulus (int8 sources have no staging ring)
     static constexpr int SMEM = 1024 + OFF_X + (X_STAGES > 0 ? X_STAGES : 0) * X_STAGE;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "MMA N");
     static_assert(NCOL % 16 == 0 && (EPI != EPI_QKV || NCOL == 64), "epilogue column split");
@@ -89,15 +90,24 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
+    int lut_in_range = 1;
     if (Cfg::SLUT && a.Lphi)
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x) { const int x0 = __ldg(a.Lphi + i), x1 = __ldg(a.Lphi + i + 1); s_lut[i] = make_int2(x0, x1 - x0); }
+        for (int i = threadIdx.x; i < LUT_S_ENTRIES; i += blockDim.x) {
+            int2 v = make_int2(i == 0 ? 0 : 65536, 0);
+            if (i > 0 && i <= 2048) {
+                const int x0 = __ldg(a.Lphi + i - 1), x1 = __ldg(a.Lphi + i);
+                v = make_int2(x0, x1 - x0);
+                lut_in_range &= x0 >= 0 && x0 <= 65536 && x1 >= 0 && x1 <= 65536;
+            }
+            s_lut[i] = v;
+        }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&a.tmW);
         if (SRC == SRC_I8) { tma_prefetch_desc(&a.tmA_hi); tma_prefetch_desc(&a.tmA_lo); }
         if (REG && a.xtma) tma_prefetch_desc(&a.tmX);
     }
     tc_fence_before();
-    __syncthreads();
+    lut_in_range = __syncthreads_and(lut_in_range);
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -163,8 +173,8 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 if (SRC == SRC_CONV32) { cb = m0 / a.conv_rows_per_img; cy0 = (m0 - cb * a.conv_rows_per_img) / a.Wo; }
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int k = (kb0 + i) * Cfg::BK;
-                    const int xs = g % Cfg::X_STAGES;
-                    if (!mbar_wait(&xempty[xs], ((g / Cfg::X_STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    const int xs = g % Cfg::XR;
+                    if (!mbar_wait(&xempty[xs], ((g / Cfg::XR) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
                     mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
                     #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
@@ -205,9 +215,9 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             const bool e15 = __all_sync(0xffffffffu, er <= 15);      // every row of the warp: the two-operation rounding
             for (int i = 0; i < nk; ++i, ++g) {
                 int4 v[8];
-                const int xs = g % Cfg::X_STAGES;
+                const int xs = g % Cfg::XR;
                 if (a.xtma) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::X_STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL))) { ok = false; break; }
+                    if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::XR) & 1, a.err, DEVERR_TIMEOUT_FULL))) { ok = false; break; }
                     const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
                     #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
@@ -264,7 +274,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
         const int et = threadIdx.x - Cfg::EPI_WARP0 * 32;
         const int q = warp & 3, hq = ew >> 2;            // TMEM lane quarter (fixed by warp % 4), column slice
         const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
-        const int2* lut = (Cfg::SLUT && a.Lphi) ? s_lut : nullptr;
+        const int2* lut = (Cfg::SLUT && a.Lphi && lut_in_range) ? s_lut : nullptr;   // else the table in global memory
         uint8_t* yb = (Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 : nullptr;
         bool ok = true;
         int tl = 0;
