@@ -45,20 +45,6 @@ struct GemmArgs {
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }
 
-// lut16 / lut_act (intops.cuh) from the table staged in shared memory with sentinels: T[0] = (0, 0) for x below
-// the range, T[1 + i] = (L[i], L[i+1] - L[i]) for i < 2048, T[2049] = (65536, 0) above it, so the range tests
-// become one clamp of the index ((x >> 10) + 1024 = (x + 2^20) >> 10 without the overflow of the sum).
-// Staged only when every L[i] lies in [0, 65536]: then x * lut(x) / 2^16 never exceeds |x| and needs no saturation.
-constexpr int LUT_S_ENTRIES = 2050;
-__device__ __forceinline__ int lut16_s(int x, const int2* __restrict__ T) {
-    const int2 e = T[min(max((x >> 10) + 1024, -1), 2048) + 1];
-    return e.x + ((e.y * (x & 1023)) >> 10);
-}
-__device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ T) {
-    const i64 t = i64(x) * lut16_s(x, T) + 32768;
-    return int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), 16));
-}
-
 // Epilogue of one 128 x BN tile for one thread = one output row (rl) and the NC columns [c0, c0 + NC) of the tile
 // (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
 // applies the per-column constants (cst[j] = column n0 + j) and writes the epilogue's outputs.  er is the row's

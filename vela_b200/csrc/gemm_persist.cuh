@@ -91,16 +91,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
     }
     if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
     int lut_in_range = 1;
-    if (Cfg::SLUT && a.Lphi)
-        for (int i = threadIdx.x; i < LUT_S_ENTRIES; i += blockDim.x) {
-            int2 v = make_int2(i == 0 ? 0 : 65536, 0);
-            if (i > 0 && i <= 2048) {
-                const int x0 = __ldg(a.Lphi + i - 1), x1 = __ldg(a.Lphi + i);
-                v = make_int2(x0, x1 - x0);
-                lut_in_range &= x0 >= 0 && x0 <= 65536 && x1 >= 0 && x1 <= 65536;
-            }
-            s_lut[i] = v;
-        }
+    if (Cfg::SLUT && a.Lphi) lut_in_range = stage_lut_s(s_lut, a.Lphi);
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&a.tmW);
         if (SRC == SRC_I8) { tma_prefetch_desc(&a.tmA_hi); tma_prefetch_desc(&a.tmA_lo); }

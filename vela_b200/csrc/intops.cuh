@@ -101,6 +101,37 @@ __device__ __forceinline__ int lut16(i64 x, const int32_t* __restrict__ L) {
 // x * lut(x) / 2^16, rounded and saturated: SiLU / GELU of a Q16 value
 __device__ __forceinline__ int lut_act(int x, const int32_t* __restrict__ L) { return int(rshr_pos(i64(x) * lut16(x, L), 16)); }
 
+// lut16 / lut_act from the table staged in shared memory with sentinels: T[0] = (0, 0) for x below
+// the range, T[1 + i] = (L[i], L[i+1] - L[i]) for i < 2048, T[2049] = (65536, 0) above it, so the range tests
+// become one clamp of the index ((x >> 10) + 1024 = (x + 2^20) >> 10 without the overflow of the sum).
+// Staged only when every L[i] lies in [0, 65536]: then x * lut(x) / 2^16 never exceeds |x| and needs no saturation.
+constexpr int LUT_S_ENTRIES = 2050;
+__device__ __forceinline__ int lut16_s(int x, const int2* __restrict__ T) {
+    const int2 e = T[min(max((x >> 10) + 1024, -1), 2048) + 1];
+    return e.x + ((e.y * (x & 1023)) >> 10);
+}
+__device__ __forceinline__ int lut_act_s(int x, const int2* __restrict__ T) {
+    const i64 t = i64(x) * lut16_s(x, T) + 32768;
+    return int(__funnelshift_r(uint32_t(t), uint32_t(t >> 32), 16));
+}
+// the same activation for a table with entries outside [0, 65536]: saturating
+__device__ __forceinline__ int lut_act_s_sat(int x, const int2* __restrict__ T) { return int(rshr_pos(i64(x) * lut16_s(x, T), 16)); }
+// stage the sentinel table T[LUT_S_ENTRIES] from L[2049] (block-strided); returns this thread's part of the
+// "every entry in [0, 65536]" test, to be and-reduced over the block
+__device__ __forceinline__ int stage_lut_s(int2* T, const int32_t* __restrict__ L) {
+    int in_range = 1;
+    for (int i = threadIdx.x; i < LUT_S_ENTRIES; i += blockDim.x) {
+        int2 v = make_int2(i == 0 ? 0 : 65536, 0);
+        if (i > 0 && i <= 2048) {
+            const int x0 = __ldg(L + i - 1), x1 = __ldg(L + i);
+            v = make_int2(x0, x1 - x0);
+            in_range &= x0 >= 0 && x0 <= 65536 && x1 >= 0 && x1 <= 65536;
+        }
+        T[i] = v;
+    }
+    return in_range;
+}
+
 // Exact floor(sqrt(v)) for 0 <= v < 2^62: double seed, then integer correction.
 __host__ __device__ __forceinline__ i64 isqrt(i64 v) {
     if (v <= 0) return 0;

@@ -211,33 +211,36 @@ __global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den) {
     gs[i] = s;
 }
 // Normalisation constants of one (sample, group) or one row, for the exact binary64 division of norm_val.
-struct NormP { double mean, scale, sd, D, rcp; };
+// c = 1.5 * 2^52 + mean (exact: |mean| < 2^31), scale = 2^(25-e), D = 2 sd, rcp = 1 / D rounded.
+constexpr double MAGIC52 = 6755399441055744.0;   // 1.5 * 2^52: integers k with |k| < 2^51 sit in its low mantissa bits
+struct NormP { double c, scale, sd, D, rcp; };
 __device__ __forceinline__ NormP norm_params(i64 mean, int e, i64 sd) {
     NormP p;
-    p.mean = double(mean); p.scale = double(i64(1) << (25 - e)); p.sd = double(sd); p.D = 2.0 * double(sd); p.rcp = 1.0 / p.D;
+    p.c = MAGIC52 + double(mean); p.scale = double(i64(1) << (25 - e)); p.sd = double(sd); p.D = 2.0 * double(sd); p.rcp = 1.0 / p.D;
     return p;
 }
-// normalise one value: sat32(rshr(floor((d * 2^(25-e) + sd) / (2 sd)) * g, 16) + beta), d = x - mean.
+// normalise one value: sat32(sat32(rshr(floor((d * 2^(25-e) + sd) / (2 sd)) * g, 16)) + beta), d = x - mean.
 // The quotient is formed in binary64, where every intermediate is an integer below 2^53: |d| <= the group's
-// range m < 2^(20+e) (2^33 when e = 12), so |d 2^(25-e)| < 2^46; the rounded product with the rounded 1/(2 sd)
-// is within 2^-6 of the true quotient, so one exact residual test (fma) corrects its floor.  sd >= 1 always
-// (sd = 0 would need var + eps = 0, impossible: a constant group has e = 0 and eps > 0).
+// range m < 2^(20+e) (2^33 when e = 12), so |d 2^(25-e)| < 2^46.  No conversion instruction is needed: the bits
+// of 1.5*2^52 + x are x in the low word and 0x43380000 (minus the sign) in the high word, so x - mean is one
+// exact subtraction of c; the quotient is rounded to an integer by adding 1.5*2^52 in the same fma, which puts
+// it in the low word of the sum.  That rounding of num * rcp (within 2^-28 of num / D) is the floor or the floor
+// plus one, and one exact residual test (fma) settles it.  sd >= 1 always (sd = 0 would need var + eps = 0,
+// impossible: a constant group has e = 0 and eps > 0).
 __device__ __forceinline__ int norm_val(int x, const NormP& p, int g, int beta) {
-    const double num = fma(double(x) - p.mean, p.scale, p.sd);
-    double q = floor(num * p.rcp);
-    const double r = fma(-q, p.D, num);
-    if (r < 0.0) q -= 1.0;
-    else if (r >= p.D) q += 1.0;
-    return int(sat32(rshr_pos(i64(q) * g, 16) + beta));
+    const double xb = __hiloint2double(0x43380000 + (x >> 31), x);     // 1.5 * 2^52 + x
+    const double num = fma(xb - p.c, p.scale, p.sd);
+    const double t = fma(num, p.rcp, MAGIC52);
+    int q = __double2loint(t);
+    const double r = fma(-(t - MAGIC52), p.D, num);
+    q += int(r >= p.D) - int(r < 0.0);
+    const i64 u = i64(q) * g + 32768;
+    const int lo = int(__funnelshift_r(uint32_t(u), uint32_t(u >> 32), 16));
+    return add_sat((int(u >> 32) >> 16) == (lo >> 31) ? lo : (u < 0 ? INT_MIN : INT_MAX), beta);
 }
-// SiLU: sat32(rshr(x lut16(x), 16)), lut16 from the table staged in shared memory as (L[i], L[i+1] - L[i])
-__device__ __forceinline__ int silu_s(int x, const int2* __restrict__ L2) {
-    int l;
-    if (x < -(16 << 16)) l = 0;
-    else if (x >= (16 << 16)) l = 65536;
-    else { const int z = x + (16 << 16); const int2 t = L2[z >> 10]; l = t.x + ((t.y * (z & 1023)) >> 10); }
-    return int(rshr_pos(i64(x) * l, 16));
-}
+// SiLU: sat32(rshr(x lut16(x), 16)), lut16 from the sentinel table staged in shared memory (lut16_s); without the
+// saturation when every table entry lies in [0, 65536] (then |result| <= |x|)
+__device__ __forceinline__ int silu_s(int x, const int2* __restrict__ T, bool in_range) { return in_range ? lut_act_s(x, T) : lut_act_s_sat(x, T); }
 // Apply.  Block = PT x RP threads over rowsPerBlock consecutive rows, GN_RPT rows per thread: a thread owns the
 // channel pairs pr, pr + PT, ... (int2; PT = min(C/2, 512)); the pair's group constants (one group unless C/32
 // is odd and the pair straddles two) of the samples the block touches (at most GN_SPAN) are staged in shared
@@ -250,12 +253,12 @@ __global__ void __launch_bounds__(512) gn_apply_kernel(const int32_t* __restrict
                                                        const int32_t* __restrict__ g, const int32_t* __restrict__ beta, const int32_t* __restrict__ Lsig,
                                                        int32_t* __restrict__ Y, u32* __restrict__ pm, int8_t* __restrict__ hi, int8_t* __restrict__ lo,
                                                        int32_t* __restrict__ e, int Kp, int rowsPerBlock) {
-    __shared__ int2 s_lut[2048];
+    __shared__ int2 s_lut[LUT_S_ENTRIES];
     __shared__ NormP s_p[GN_SPAN][32];
     __shared__ u32 s_rmax[256];
     extern __shared__ int32_t s_rows[];            // QUANT: [rowsPerBlock][C]
     const int P2 = C >> 1, PT = min(P2, 512), RP = blockDim.x / PT, cg = C >> 5;
-    if (Lsig) for (int i = threadIdx.x; i < 2048; i += blockDim.x) { const int x0 = __ldg(Lsig + i), x1 = __ldg(Lsig + i + 1); s_lut[i] = make_int2(x0, x1 - x0); }
+    const bool lut_in_range = __syncthreads_and(Lsig ? stage_lut_s(s_lut, Lsig) : 1);
     const int rr = threadIdx.x / PT;
     // PT % 32 == 0 (C % 64 == 0, every UNet width): a warp's lanes share the row, so its row max is reduced first
     const bool warp_rows = (PT & 31) == 0;
@@ -285,7 +288,7 @@ __global__ void __launch_bounds__(512) gn_apply_kernel(const int32_t* __restrict
                     if (sl != cur) { p0 = s_p[sl][g0]; p1 = s_p[sl][g1]; cur = sl; }
                     const int2 xv = __ldg(reinterpret_cast<const int2*>(X + size_t(r) * C + c));
                     int v0 = norm_val(xv.x, p0, gv.x, bv.x), v1 = norm_val(xv.y, p1, gv.y, bv.y);
-                    if (Lsig) { v0 = silu_s(v0, s_lut); v1 = silu_s(v1, s_lut); }
+                    if (Lsig) { v0 = silu_s(v0, s_lut, lut_in_range); v1 = silu_s(v1, s_lut, lut_in_range); }
                     if constexpr (QUANT) *reinterpret_cast<int2*>(s_rows + (r - r0) * C + c) = make_int2(v0, v1);
                     else *reinterpret_cast<int2*>(Y + size_t(r) * C + c) = make_int2(v0, v1);
                     u32 m = max(uabs(v0), uabs(v1));
