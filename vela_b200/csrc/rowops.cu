@@ -143,11 +143,16 @@ __device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean
 template <int PASS>
 __global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
     __shared__ long long sacc[32]; __shared__ int smn[32], smx[32]; __shared__ long long smean[32]; __shared__ int se[32];
+    __shared__ bool sfast[32];
     const int Q = C >> 2, RP = blockDim.x / Q, cg = C >> 5;
     const int b = blockIdx.y, t0 = blockIdx.x * rowsPerBlock, t1 = min(T, t0 + rowsPerBlock);
     if (threadIdx.x < 32) {
         sacc[threadIdx.x] = 0; smn[threadIdx.x] = INT_MAX; smx[threadIdx.x] = INT_MIN;
-        if (PASS == 2) { i64 mean; int e; gn_mean_e(gs[b * 32 + threadIdx.x], i64(T) * cg, mean, e); smean[threadIdx.x] = mean; se[threadIdx.x] = e; }
+        if (PASS == 2) {
+            const vela_gnstat g = gs[b * 32 + threadIdx.x];
+            i64 mean; int e; gn_mean_e(g, i64(T) * cg, mean, e); smean[threadIdx.x] = mean; se[threadIdx.x] = e;
+            sfast[threadIdx.x] = max(i64(g.mx) - mean, mean - i64(g.mn)) < (i64(1) << 30);
+        }
     }
     __syncthreads();
     const int c4 = threadIdx.x % Q, rr = threadIdx.x / Q;
@@ -156,6 +161,12 @@ __global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restric
         int gi[4]; i64 mean[4] = {0, 0, 0, 0}; int e[4] = {0, 0, 0, 0};
         #pragma unroll
         for (int k = 0; k < 4; ++k) { gi[k] = (c + k) / cg; if (PASS == 2) { mean[k] = smean[gi[k]]; e[k] = se[gi[k]]; } }
+        // pass 2 with every deviation below 2^30 in magnitude (the groups' ranges, checked in the prologue): the
+        // rounded deviation (d + 2^(e-1)) >> e and its square accumulate in 32 / 64 bits without 64-bit shifts
+        bool small = PASS == 2;
+        int mean32[4], half[4];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) { small = small && sfast[gi[k]]; mean32[k] = int(mean[k]); half[k] = e[k] ? 1 << (e[k] - 1) : 0; }
         i64 acc[4] = {0, 0, 0, 0}; int mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
         const int32_t* x = X + (size_t(b) * T) * C + c;
         auto take = [&](const int4 v) {
@@ -163,6 +174,7 @@ __global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restric
             #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 if (PASS == 1) { acc[k] += vv[k]; mn[k] = min(mn[k], vv[k]); mx[k] = max(mx[k], vv[k]); }
+                else if (small) { const int dd = (vv[k] - mean32[k] + half[k]) >> e[k]; acc[k] += i64(dd) * dd; }
                 else { const i64 d = i64(vv[k]) - mean[k]; const i64 dd = e[k] ? ((d >> e[k]) + ((d >> (e[k] - 1)) & 1)) : d; acc[k] += dd * dd; }
             }
         };
@@ -346,11 +358,21 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
     const i64 rng = max(i64(mx) - mean, mean - i64(mn));
     const int ex = max(0, (rng >= (i64(1) << 32) ? 17 : row_exp(u32(rng))) - 5);
     i64 ss = 0;
-    #pragma unroll
-    for (int j = 0; j < R4; ++j) {
-        if (lane + 32 * j >= C4) break;
+    if (rng < (i64(1) << 30)) {            // every deviation below 2^30: rounded shift and square in 32 / 64 bits
+        const int m32 = int(mean), h = ex ? 1 << (ex - 1) : 0;
         #pragma unroll
-        for (int k = 0; k < 4; ++k) { const i64 d = i64(v[4 * j + k]) - mean; const i64 dd = ex ? ((d >> ex) + ((d >> (ex - 1)) & 1)) : d; ss += dd * dd; }
+        for (int j = 0; j < R4; ++j) {
+            if (lane + 32 * j >= C4) break;
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) { const int dd = (v[4 * j + k] - m32 + h) >> ex; ss += i64(dd) * dd; }
+        }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < R4; ++j) {
+            if (lane + 32 * j >= C4) break;
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) { const i64 d = i64(v[4 * j + k]) - mean; const i64 dd = ex ? ((d >> ex) + ((d >> (ex - 1)) & 1)) : d; ss += dd * dd; }
+        }
     }
     ss = warp_sum64(ss);
     const i64 var = floor_div_inv(ss, uint64_t(n), k.inv_n);
@@ -363,10 +385,18 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
     for (int j = 0; j < R4; ++j) {
         const int c4 = lane + 32 * j;
         if (c4 >= C4) break;
+        int gv[4], bv[4];
+        if (sizeof(GT) == 4 && ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0) {
+            const int4 g4 = __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const int32_t*>(g) + c4 * 4));
+            const int4 b4 = __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const int32_t*>(beta) + c4 * 4));
+            gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w; bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+        } else {
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) { gv[k] = int(g[c4 * 4 + k]); bv[k] = int(beta[c4 * 4 + k]); }
+        }
         #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int c = c4 * 4 + k;
-            v[4 * j + k] = norm_val(v[4 * j + k], np, int(g[c]), int(beta[c]));
+            v[4 * j + k] = norm_val(v[4 * j + k], np, gv[k], bv[k]);
             m = max(m, uabs(v[4 * j + k]));
         }
         if (!QUANT) *reinterpret_cast<int4*>(Y + size_t(r) * C + c4 * 4) = make_int4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
