@@ -186,7 +186,7 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
 
 __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sm = align_smem_1024(smem_raw);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1; uint64_t* k_empty = k_full + KS;

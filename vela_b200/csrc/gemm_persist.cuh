@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
     using Cfg = PersistCfg<BN, STAGES, SRC, EPI>;
     constexpr bool REG = Cfg::REG;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = align_smem_1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE);
     uint64_t* empty = full + STAGES;
     uint64_t* accf = empty + STAGES;            // [2] accumulator buffer b holds a finished tile

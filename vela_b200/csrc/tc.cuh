@@ -42,6 +42,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return true;
 }
 
+// The dynamic shared-memory base rounded up to 1024 bytes (the 128-byte swizzle atom), formed as an offset of the
+// __shared__ array itself so the compiler keeps the shared address space (shared loads / stores, not generic ones).
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* raw) {
+    const uint32_t a = smem_u32(raw);
+    return raw + (((a + 1023u) & ~1023u) - a);
+}
+
 // ---- TMA (no multicast anywhere in this library) ----
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(m)) : "memory");
