@@ -140,8 +140,12 @@ __device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean
 // Statistics passes.  Block = Q x RP threads (Q = C / 4 column quads, RP row lanes); a thread keeps one quad
 // (four channels, fixed groups) over every RP-th row of the block's rows, four rows in flight, then the block
 // combines per group in shared memory and adds to the (sample, group) record once.
+// Pass 2 also finishes the records: every block counts itself in gs[0].pad_ (zeroed by gn_init) after its
+// atomics, and the block that counts last (no block waits for another) derives mean, e and sd of all B x 32
+// records and clears the counter.
 template <int PASS>
-__global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs) {
+__global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restrict__ X, int T, int C, int rowsPerBlock, vela_gnstat* gs,
+                                                        int cnt, i64 den) {
     __shared__ long long sacc[32]; __shared__ int smn[32], smx[32]; __shared__ long long smean[32]; __shared__ int se[32];
     __shared__ bool sfast[32];
     const int Q = C >> 2, RP = blockDim.x / Q, cg = C >> 5;
@@ -208,19 +212,32 @@ __global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restric
             atomicAdd(reinterpret_cast<unsigned long long*>(&st->ss), (unsigned long long)sacc[threadIdx.x]);
         }
     }
+    if constexpr (PASS == 2) {
+        __shared__ bool s_last;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned done = atomicAdd(reinterpret_cast<unsigned*>(&gs[0].pad_), 1u);
+            s_last = done == gridDim.x * gridDim.y - 1;
+        }
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            const i64 n = i64(T) * cg;
+            for (int i = threadIdx.x; i < cnt; i += blockDim.x) gn_finish_one(gs + i, n, den);
+        }
+    }
 }
 // mean, e, ss -> var, eps, sd (src/kernels.cu:204-211)
-__global__ void gn_finish_kernel(vela_gnstat* gs, int cnt, i64 n, i64 den) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= cnt) return;
-    vela_gnstat s = gs[i];
+__device__ __forceinline__ void gn_finish_one(vela_gnstat* g, i64 n, i64 den) {
+    vela_gnstat s = *g;
     i64 mean; int e; gn_mean_e(s, n, mean, e);
-    s.mean = mean; s.e = e;
+    s.mean = mean; s.e = e; s.pad_ = 0;
     const i64 var = floor_div(s.ss, n);
     const int sh = 32 - 2 * e; const i64 one = sh >= 0 ? (i64(1) << sh) : 0;
     const i64 eps = floor_div(one + den / 2, den);
     s.sd = isqrt((var + eps) << 16);
-    gs[i] = s;
+    *g = s;
 }
 // Normalisation constants of one (sample, group) or one row, for the exact binary64 division of norm_val.
 // c = 1.5 * 2^52 + mean (exact: |mean| < 2^31), scale = 2^(25-e), D = 2 sd, rcp = 1 / D rounded.
@@ -592,9 +609,8 @@ void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, v
     const int rpb = ceil_div(T, chunks);
     gn_init_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt);
     const dim3 grid(ceil_div(T, rpb), B);
-    gn_stats_kernel<1><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs);
-    gn_stats_kernel<2><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs);
-    gn_finish_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt, i64(T) * (C / 32), den);
+    gn_stats_kernel<1><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs, cnt, den);
+    gn_stats_kernel<2><<<grid, Q * RP, 0, st>>>(X, T, C, rpb, gs, cnt, den);     // + the finish (last block)
 }
 void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela_gnstat* gs, const int32_t* g, const int32_t* beta,
               const int32_t* Lsig, int32_t* Y, uint32_t* pm, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
