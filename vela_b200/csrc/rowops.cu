@@ -67,23 +67,29 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ X, int M, int Mpad
 }
 
 // Row quantisation with the row maxima already known (the producing epilogue's row max): one read of X.
-// Block = 256 threads over rows of K / 4 int4 quads each (K % 4 == 0); rows [M, Mpad) become value 0.
+// One warp per row (grid-stride), four columns per lane and step: the quantised quad is formed with the packed
+// saturating narrowing of quant_pack4 (the two-operation rounding for exponents up to 15) and stored as one
+// 32-bit word of hi bytes and one of lo bytes; K % 4 == 0, columns [K, Kp) and rows [M, Mpad) become value 0.
 __global__ void quant_rows_rm_kernel(const int32_t* __restrict__ X, const u32* __restrict__ rowmax, int M, int Mpad, int K, int ldx,
                                      int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
-    const int Q = Kp >> 2;                                 // output quads per row (K quads carry data, the rest is padding)
-    const size_t n = size_t(Mpad) * Q;
-    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-        const int r = int(i / Q), c = int(i - size_t(r) * Q) * 4;
-        int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
-        if (r < M) {
-            const int ee = row_exp(__ldg(rowmax + r));
-            if (c == 0) e[r] = ee;
-            if (c < K) {
-                const int4 v = __ldg(reinterpret_cast<const int4*>(X + size_t(r) * ldx + c));
-                q0 = quant16(v.x, ee); q1 = quant16(v.y, ee); q2 = quant16(v.z, ee); q3 = quant16(v.w, ee);
+    const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+    for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < Mpad; r += gridDim.x * wpb) {
+        u32* h = reinterpret_cast<u32*>(hi + size_t(r) * Kp);
+        u32* l = reinterpret_cast<u32*>(lo + size_t(r) * Kp);
+        const int ee = r < M ? row_exp(__ldg(rowmax + r)) : 0;
+        if (lane == 0) e[r] = ee;
+        const int kq = r < M ? (K >> 2) : 0;
+        const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qs2 = qr, qh = (1 << ee) >> 1;
+        const int32_t* x = X + size_t(r) * ldx;
+        for (int c4 = lane; c4 < (Kp >> 2); c4 += 32) {
+            uint32_t hw = 0u, lw = 0x80808080u;
+            if (c4 < kq) {
+                const int4 v = __ldg(reinterpret_cast<const int4*>(x) + c4);
+                if (ee <= 15) quant_pack4_e15(v.x, v.y, v.z, v.w, qh, ee, hw, lw);
+                else quant_pack4(v.x, v.y, v.z, v.w, qs1, qr, qs2, hw, lw);
             }
-        } else if (c == 0) e[r] = 0;
-        store_q4(hi + size_t(r) * Kp, lo + size_t(r) * Kp, c, q0, q1, q2, q3);
+            h[c4] = hw; l[c4] = lw;
+        }
     }
 }
 
@@ -589,8 +595,7 @@ void quant_rows(cudaStream_t st, const int32_t* X, int M, int K, int ldx, int8_t
 void quant_rows_rm(cudaStream_t st, const int32_t* X, const uint32_t* rowmax, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int Mpad) {
     VELA_REQUIRE(X && rowmax && hi && lo && e && M > 0 && K > 0 && K % 4 == 0 && ldx % 4 == 0 && Kp >= K && Kp % 4 == 0 && Mpad >= M,
                  "quant_rows_rm: needs K, ldx and Kp multiples of 4");
-    const size_t n = size_t(Mpad) * (Kp / 4);
-    quant_rows_rm_kernel<<<unsigned(std::min<size_t>((n + 255) / 256, size_t(sm_count()) * 16)), 256, 0, st>>>(X, rowmax, M, Mpad, K, ldx, hi, lo, e, Kp);
+    quant_rows_rm_kernel<<<unsigned(std::min(ceil_div(Mpad, 8), sm_count() * 16)), 256, 0, st>>>(X, rowmax, M, Mpad, K, ldx, hi, lo, e, Kp);
 }
 void pixmax(cudaStream_t st, const int32_t* X, int rows, int C, uint32_t* pm) {
     VELA_REQUIRE(X && pm && rows > 0 && C > 0, "pixmax: bad arguments");
