@@ -143,6 +143,17 @@ __device__ __forceinline__ void gn_mean_e(const vela_gnstat& s, i64 n, i64& mean
     const i64 m = max(i64(s.mx) - mean, mean - i64(s.mn));
     e = max(0, (m >= (i64(1) << 32) ? 17 : row_exp(u32(m))) - 5);
 }
+// mean, e, ss -> var, eps, sd (src/kernels.cu:204-211)
+__device__ __forceinline__ void gn_finish_one(vela_gnstat* g, i64 n, i64 den) {
+    vela_gnstat s = *g;
+    i64 mean; int e; gn_mean_e(s, n, mean, e);
+    s.mean = mean; s.e = e; s.pad_ = 0;
+    const i64 var = floor_div(s.ss, n);
+    const int sh = 32 - 2 * e; const i64 one = sh >= 0 ? (i64(1) << sh) : 0;
+    const i64 eps = floor_div(one + den / 2, den);
+    s.sd = isqrt((var + eps) << 16);
+    *g = s;
+}
 // Statistics passes.  Block = Q x RP threads (Q = C / 4 column quads, RP row lanes); a thread keeps one quad
 // (four channels, fixed groups) over every RP-th row of the block's rows, four rows in flight, then the block
 // combines per group in shared memory and adds to the (sample, group) record once.
@@ -234,17 +245,7 @@ __global__ void __launch_bounds__(1024) gn_stats_kernel(const int32_t* __restric
         }
     }
 }
-// mean, e, ss -> var, eps, sd (src/kernels.cu:204-211)
-__device__ __forceinline__ void gn_finish_one(vela_gnstat* g, i64 n, i64 den) {
-    vela_gnstat s = *g;
-    i64 mean; int e; gn_mean_e(s, n, mean, e);
-    s.mean = mean; s.e = e; s.pad_ = 0;
-    const i64 var = floor_div(s.ss, n);
-    const int sh = 32 - 2 * e; const i64 one = sh >= 0 ? (i64(1) << sh) : 0;
-    const i64 eps = floor_div(one + den / 2, den);
-    s.sd = isqrt((var + eps) << 16);
-    *g = s;
-}
+
 // Normalisation constants of one (sample, group) or one row, for the exact binary64 division of norm_val.
 // c = 1.5 * 2^52 + mean (exact: |mean| < 2^31), scale = 2^(25-e), D = 2 sd, rcp = 1 / D rounded.
 constexpr double MAGIC52 = 6755399441055744.0;   // 1.5 * 2^52: integers k with |k| < 2^51 sit in its low mantissa bits
