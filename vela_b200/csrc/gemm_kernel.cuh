@@ -66,6 +66,13 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             for (int j = 0; j < 16; ++j) { const int4 cc = cst[c0 + c * 16 + j]; y[c * 16 + j] = FAST ? epi_y_fast(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)) : epi_y(hi[j], lo[j], cc.x, cc.y - er, cc.z, ws128(cc)); }
         }
         const int nh = n0 + c0;
+        // the head's row exponent and the warp's choice of rounding form, voted by every lane (rows past Mreal vote
+        // for the short form) before the per-lane branch below
+        u32 hm = 0;
+        #pragma unroll
+        for (int j = 0; j < 64; ++j) hm = max(hm, uabs(y[j]));
+        const int ee = row_exp(hm);
+        const bool e15 = __all_sync(0xffffffffu, !live || ee <= 15);
         if (live && nh < a.Nreal) {
             const int part = nh / a.Cq, head = (nh - part * a.Cq) >> 6;
             if (part == 2) {
@@ -73,30 +80,30 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                 #pragma unroll
                 for (int j = 0; j < 16; ++j) dst[j] = make_int4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
             } else {
-                u32 m = 0;
-                #pragma unroll
-                for (int j = 0; j < 64; ++j) m = max(m, uabs(y[j]));
-                const int ee = row_exp(m);
                 const int b = grow / a.T, t = grow - b * a.T;
                 const int Tp = part == 0 ? a.TpQ : a.TpK;
                 const size_t gt = size_t(b * a.heads + head) * Tp + t;
                 int8_t* hip = (part == 0 ? a.qhi : a.khi) + gt * 64; int8_t* lop = (part == 0 ? a.qlo : a.klo) + gt * 64;
-                int hs = 0, ls = 0, ts = 0;
+                // quant16 of the head's 64 values, four at a time into hi / lo byte words (quant_pack4; the two-operation
+                // rounding when every live row of the warp has e <= 15); the plane sums from the packed bytes (dp4a), and
+                // sum q = 256 sum hi + sum lo + 128 * 64 since q = 256 hi + lo + 128
+                const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
+                int hs = 0, ls = 0;
                 #pragma unroll
                 for (int j = 0; j < 16; j += 4) {
                     uint32_t hw[4], lw[4];
                     #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int b4 = (j + u) * 4;
-                        const int q0 = quant16(y[b4], ee), q1 = quant16(y[b4 + 1], ee), q2 = quant16(y[b4 + 2], ee), q3 = quant16(y[b4 + 3], ee);
-                        hw[u] = pack_hi4(q0, q1, q2, q3); lw[u] = pack_lo4(q0, q1, q2, q3);
-                        hs += (q0 >> 8) + (q1 >> 8) + (q2 >> 8) + (q3 >> 8);
-                        ls += ((q0 & 255) - 128) + ((q1 & 255) - 128) + ((q2 & 255) - 128) + ((q3 & 255) - 128);
-                        ts += q0 + q1 + q2 + q3;
+                        if (e15) quant_pack4_e15(y[b4], y[b4 + 1], y[b4 + 2], y[b4 + 3], qh, ee, hw[u], lw[u]);
+                        else quant_pack4(y[b4], y[b4 + 1], y[b4 + 2], y[b4 + 3], qs1, qr, qr, hw[u], lw[u]);
+                        hs = __dp4a(int(hw[u]), 0x01010101, hs);
+                        ls = __dp4a(int(lw[u]), 0x01010101, ls);
                     }
                     *reinterpret_cast<uint4*>(hip + j * 4) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                     *reinterpret_cast<uint4*>(lop + j * 4) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                 }
+                const int ts = 256 * hs + ls + 128 * 64;
                 (part == 0 ? a.qe : a.ke)[gt] = ee;
                 (part == 0 ? a.qhs : a.khs)[gt] = hs;
                 (part == 0 ? a.qls : a.kls)[gt] = ls;
