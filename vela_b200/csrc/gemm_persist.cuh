@@ -1,11 +1,11 @@
 // Persistent W8A16 GEMM on the sm_100a tensor cores: one CTA per SM walks the output tiles
 // t = blockIdx.x, blockIdx.x + gridDim.x, ... (column tiles fastest, so the CTAs in flight share A rows in L2).
 //
-// Same arithmetic, operand sources and epilogues as gemm_w8a16_kernel (gemm_kernel.cuh); what changes is the
-// schedule.  Two TMEM accumulator buffers (2 x [hi | lo] x BN columns) let the epilogue of tile i run while the
-// MMAs of tile i+1 accumulate, and the TMA / converter rings run continuously across tile boundaries, so the
-// short-K GEMMs of the UNet (K = 320..1280, 5-20 k-blocks per tile) no longer pay a pipeline fill, a TMEM
-// allocation and an exposed epilogue per tile.
+// The arithmetic, operand sources and epilogues are those of gemm_kernel.cuh; this file is the schedule.  Two
+// TMEM accumulator buffers (2 x [hi | lo] x BN columns, when 4 BN <= 512) let the epilogue of tile i run while
+// the MMAs of tile i+1 accumulate, and the TMA / converter rings run continuously across tile boundaries, so
+// the short-K GEMMs of the UNet (K = 320..1280, 5-20 k-blocks per tile) pay no pipeline fill and no TMEM
+// allocation per tile.
 //
 // Warp roles (THREADS = 32 x (2 + NCW + EW + XW)):
 //   warp 0            TMA producer: W (and the A-hi / A-lo planes of int8 sources)
