@@ -563,7 +563,11 @@ __global__ void quant_v_max_kernel(const int32_t* __restrict__ X, int Tk, int C,
     __syncthreads();
     if (ts == 0) { m = max(max(sm[0][d], sm[1][d]), max(sm[2][d], sm[3][d])); if (m) atomicMax(colmax + g * 64 + d, m); }
 }
-// transposed quantised write [G][64][Tkp] + per-column sums of the true values: block = (g, 64-row t tile)
+// transposed quantised write [G][64][Tkp] + per-column sums of the quantised values: block = (g, 64-row t tile).
+// After the tile is staged, each half-warp takes one column d and its 16 lanes four consecutive t each: the four
+// values become one word of hi bytes and one of lo bytes (quant_pack4), stored at t..t+3 of row d, and the sum
+// of q over them is 256 * (hi byte sum) + (lo byte sum) + 4 * 128 (q = 256 hi + lo + 128; dp4a byte sums),
+// reduced over the half-warp before one atomic per column.  Padded t (>= Tk) hold 0 and quantise to 0.
 __global__ void quant_v_write_kernel(const int32_t* __restrict__ X, int Tk, int C, int heads, int Tkp, const u32* __restrict__ colmax,
                                      int8_t* __restrict__ vh, int8_t* __restrict__ vl, int32_t* __restrict__ ev, i64* __restrict__ vsum) {
     __shared__ int tile[64][65];
@@ -571,16 +575,20 @@ __global__ void quant_v_write_kernel(const int32_t* __restrict__ X, int Tk, int 
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
     for (int r = ty; r < 64; r += 4) { const int t = t0 + r; tile[r][tx] = t < Tk ? __ldg(X + (size_t(b) * Tk + t) * C + h * 64 + tx) : 0; }
     __syncthreads();
-    for (int d = ty; d < 64; d += 4) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tl = lane & 15;
+    for (int d = 2 * warp + (lane >> 4); d < 64; d += 2 * (blockDim.x >> 5)) {
         const int e = row_exp(colmax[g * 64 + d]);
-        const int t = t0 + tx;
-        const int q = t < Tk ? quant16(tile[tx][d], e) : 0;
-        const size_t o = (size_t(g) * 64 + d) * Tkp + t;
-        vh[o] = int8_t(q >> 8); vl[o] = int8_t((q & 255) - 128);
-        i64 s = q;
-        for (int o2 = 16; o2; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
-        if ((tx & 31) == 0 && s) atomicAdd(reinterpret_cast<unsigned long long*>(vsum + g * 64 + d), (unsigned long long)s);
-        if (blockIdx.x == 0 && tx == 0) ev[g * 64 + d] = e;
+        const int qs1 = e > 0 ? e - 1 : 0, qr = e > 0 ? 1 : 0;
+        uint32_t hw, lw;
+        quant_pack4(tile[4 * tl][d], tile[4 * tl + 1][d], tile[4 * tl + 2][d], tile[4 * tl + 3][d], qs1, qr, qr, hw, lw);
+        const size_t o = (size_t(g) * 64 + d) * Tkp + t0 + 4 * tl;
+        *reinterpret_cast<uint32_t*>(vh + o) = hw;
+        *reinterpret_cast<uint32_t*>(vl + o) = lw;
+        int sq = 256 * __dp4a(int(hw), 0x01010101, 0) + __dp4a(int(lw), 0x01010101, 0) + 4 * 128;
+        #pragma unroll
+        for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o2);
+        if (tl == 0 && sq) atomicAdd(reinterpret_cast<unsigned long long*>(vsum + g * 64 + d), (unsigned long long)i64(sq));
+        if (blockIdx.x == 0 && tl == 0) ev[g * 64 + d] = e;
     }
 }
 
@@ -688,6 +696,7 @@ void quant_heads(cudaStream_t st, const int32_t* X, int B, int T, int C, int hea
 }
 void quant_v(cudaStream_t st, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vh, int8_t* vl, int32_t* ev, i64* vsum, uint32_t* colmax) {
     VELA_REQUIRE(X && vh && vl && ev && vsum && colmax && C == heads * 64 && Tkp >= Tk && Tkp % 64 == 0, "quant_v: bad arguments");
+    VELA_REQUIRE(((reinterpret_cast<uintptr_t>(vh) | reinterpret_cast<uintptr_t>(vl)) & 3) == 0, "quant_v: vh and vl must be 4-byte aligned");
     const int G = B * heads;
     VELA_CUDA(cudaMemsetAsync(colmax, 0, size_t(G) * 64 * 4, st));
     VELA_CUDA(cudaMemsetAsync(vsum, 0, size_t(G) * 64 * 8, st));
