@@ -343,10 +343,13 @@ __global__ void __launch_bounds__(512) gn_apply_kernel(const int32_t* __restrict
             for (int i = threadIdx.x; i < (r1 - r0) * K4; i += blockDim.x) {
                 const int rl = i / K4, c = (i - rl * K4) * 4;
                 const int ee = row_exp(s_rmax[rl]);
-                int q[4];
+                int v[4];
                 #pragma unroll
-                for (int k = 0; k < 4; ++k) q[k] = c + k < C ? quant16(s_rows[rl * C + c + k], ee) : 0;
-                store_q4(hi + size_t(r0 + rl) * Kp, lo + size_t(r0 + rl) * Kp, c, q[0], q[1], q[2], q[3]);
+                for (int k = 0; k < 4; ++k) v[k] = c + k < C ? s_rows[rl * C + c + k] : 0;
+                uint32_t hw, lw;
+                quant_pack4(v[0], v[1], v[2], v[3], ee > 0 ? ee - 1 : 0, ee > 0 ? 1 : 0, ee > 0 ? 1 : 0, hw, lw);
+                *reinterpret_cast<u32*>(hi + size_t(r0 + rl) * Kp + c) = hw;
+                *reinterpret_cast<u32*>(lo + size_t(r0 + rl) * Kp + c) = lw;
             }
         }
         __syncthreads();      // s_rmax, s_p and s_rows are reused by the next chunk
@@ -429,11 +432,17 @@ __global__ void lnorm_kernel(const int32_t* __restrict__ X, int M, int C, const 
     const int ee = row_exp(warp_umax(m));
     int8_t* h = hi + size_t(r) * Kp; int8_t* l = lo + size_t(r) * Kp;
     if (lane == 0) e[r] = ee;
+    // the row is this warp's: one rounding form for all its lanes (the two-operation one when e <= 15)
+    const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
     #pragma unroll
     for (int j = 0; j < R4; ++j) {
         const int c4 = lane + 32 * j;
         if (c4 >= C4) break;
-        store_q4(h, l, c4 * 4, quant16(v[4 * j], ee), quant16(v[4 * j + 1], ee), quant16(v[4 * j + 2], ee), quant16(v[4 * j + 3], ee));
+        uint32_t hw, lw;
+        if (ee <= 15) quant_pack4_e15(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3], qh, ee, hw, lw);
+        else quant_pack4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3], qs1, qr, qr, hw, lw);
+        *reinterpret_cast<u32*>(h + c4 * 4) = hw;
+        *reinterpret_cast<u32*>(l + c4 * 4) = lw;
     }
     pad_cols(h, l, C, Kp, lane);
 }
