@@ -262,7 +262,8 @@ __device__ __forceinline__ NormP norm_params(i64 mean, int e, i64 sd) {
 // exact subtraction of c; the quotient is rounded to an integer by adding 1.5*2^52 in the same fma, which puts
 // it in the low word of the sum.  That rounding of num * rcp (within 2^-28 of num / D) is the floor or the floor
 // plus one, and one exact residual test (fma) settles it.  sd >= 1 always (sd = 0 would need var + eps = 0,
-// impossible: a constant group has e = 0 and eps > 0).
+// impossible: a constant group has e = 0 and eps > 0), and the quotient fits 32 bits: sd = isqrt((var + eps) << 16)
+// of the group's (row's) own deviations keeps |d| 2^(24-e) / sd near 2^16 sqrt(n) at most (n <= 2^20 values).
 __device__ __forceinline__ int norm_val(int x, const NormP& p, int g, int beta) {
     const double xb = __hiloint2double(0x43380000 + (x >> 31), x);     // 1.5 * 2^52 + x
     const double num = fma(xb - p.c, p.scale, p.sd);
