@@ -49,7 +49,7 @@ __device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* raw) {
     return raw + (((a + 1023u) & ~1023u) - a);
 }
 
-// ---- TMA (no multicast anywhere in this library) ----
+// ---- TMA: every load targets this CTA's own shared memory (no cluster-wide copies in this library) ----
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
