@@ -202,6 +202,20 @@ void* vela_engine_stream(const vela_engine* e);
 double vela_engine_last_ms(const vela_engine* e);   /* device time of the last vela_engine_run, ms */
 
 /* ---------------------------------------------------------------------------------
+ * Host share hashing (the reference's mining / verify path; FIPS 180-4 SHA-256 on the host, no CUDA).
+ * ------------------------------------------------------------------------------ */
+/* sha256d(data) = SHA-256(SHA-256(data)) (meow::sha256d, src/sha256.h:84). */
+int vela_sha256d(const uint8_t* data, size_t n, uint8_t* out32);
+/* the proof-of-inference output hash of one inference: the tagged hash "POI/out" over seed[32] || x0[32768]
+ * (poiOut, src/main.cpp:79; TaggedHasher, src/sha256.h:86-91). */
+int vela_poi_out(const uint8_t* seed32, const uint8_t* x0, uint8_t* out32);
+/* vela_poi_out over a batch (seeds [batch][32], x0 [batch][32768], out [batch][32]) on up to `threads` host
+ * threads (the per-inference loop of src/main.cpp:139 and 262). */
+int vela_poi_out_batch(const uint8_t* seeds, const uint8_t* x0, int batch, int threads, uint8_t* out);
+/* the share hash: sha256d(header[80] || poi[32]) (src/main.cpp:263-264). */
+int vela_share_hash(const uint8_t* header80, const uint8_t* poi32, uint8_t* out32);
+
+/* ---------------------------------------------------------------------------------
  * Tooling (no reference counterpart): seeded random-init model in the POISDv1
  * format the reference loads (src/poisd.cpp:17-35), with every tensor of the
  * SD-2.1 UNet and 23-layer text encoder.  Host path.  ~1.19 GB.

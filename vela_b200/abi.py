@@ -35,6 +35,10 @@ SIGNATURES = {
     "vela_version": (ctypes.c_char_p, []),
     "vela_device_error": (U, [I]),
     "vela_synth_model_write": (I, [ctypes.c_char_p, U64]),
+    "vela_sha256d": (I, [P, SZ, P]),
+    "vela_poi_out": (I, [P, P, P]),
+    "vela_poi_out_batch": (I, [P, P, I, I, P]),
+    "vela_share_hash": (I, [P, P, P]),
     "vela_gemm_w8a16": (I, [P, ctypes.POINTER(ASrc), I, I, P, I, I, I, I, P, ctypes.POINTER(AEpi)]),
     "vela_gemm_hl": (I, [P, P, P, I, I, I, P, I, I, I, I, P, P, P, I, P, I, I, P, P, P]),
     "vela_conv_e": (I, [P, P, I, I, I, I, P]),

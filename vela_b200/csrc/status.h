@@ -31,4 +31,15 @@ template <class F> int guarded(const char* what, F&& body) {
         return fail(VELA_ERR_ARG, std::string(what) + ": " + ex.what());
     }
 }
+// The same for host-only entries (no CUDA state is touched or queried).
+template <class F> int guarded_host(const char* what, F&& body) {
+    try {
+        body();
+        return VELA_OK;
+    } catch (const Error& ex) {
+        return fail(ex.code, std::string(what) + ": " + ex.what());
+    } catch (const std::exception& ex) {
+        return fail(VELA_ERR_ARG, std::string(what) + ": " + ex.what());
+    }
+}
 }  // namespace vela
