@@ -202,6 +202,27 @@ def test_x32_ragged_k(M, K, N):
     assert np.array_equal(H(Y), exp)
 
 
+@pytest.mark.parametrize("M,N,ldy", [(150, 200, 204), (150, 200, 201), (37, 72, 76)])
+def test_plain_ragged_n_strided_y(M, N, ldy):
+    """plain epilogue (+ residual + row max) with N not a multiple of 16 into a strided Y: the last 16-column chunk
+    is partial (shared-memory box + TMA store clipped at N when ldy % 4 == 0, per-element stores otherwise), and the
+    columns [N, ldy) and the rows past M keep their contents"""
+    rng = np.random.default_rng(M + N + ldy); d = Dev()
+    K = 320; Np = (N + 15) // 16 * 16; Mp = (M + 63) // 64 * 64
+    q = rng.integers(-32768, 32768, (Mp, K))
+    Ahi = (q >> 8).astype(np.int8); Alo = ((q & 255) - 128).astype(np.int8)
+    W = rng.integers(-127, 128, (Np, K)).astype(np.int8)
+    c = cst_for(rng, W, N, Np); e = rng.integers(0, 8, Mp).astype(np.int32)
+    R = np.zeros((M, ldy), np.int32); R[:, :N] = rbits(rng, (M, N), 30)
+    Y = d.empty((M + 3, ldy), torch.int32, 0x5A); rm = d.zeros(Mp, torch.int32)
+    E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = A(Y); E.ldy = ldy; E.residual = A(d(R)); E.rowmax = A(rm)
+    run_gemm(planar_src(d(Ahi), d(Alo), K, d(e)), Mp, M, d(W), K, Np, N, K, d(c), E)
+    exp = np.full((M + 3, ldy), np.int32(0x5A5A5A5A), np.int32); erm = np.zeros(M, np.uint32)
+    O.gemm_hl(Ahi, Alo, M, W, N, K, c, e, O.EPI_PLAIN, Y=exp, ldy=ldy, residual=R, rowmax=erm)
+    assert np.array_equal(H(Y), exp)
+    assert np.array_equal(H(rm)[:M].view(np.uint32), erm)
+
+
 def test_config1_shape():
     """config 1: A 16-bit uniform over [-32768, 32767] as planes, M 4096, N = K = 320, e in [0, 12)."""
     rng = np.random.default_rng(1); d = Dev()
