@@ -92,6 +92,9 @@ class Ranks:
         if self.world > 1:
             import datetime
             import torch.distributed as dist
+            # NCCL's own messages (its version banner when NCCL_DEBUG is set) go to a per-rank file in the temp
+            # directory, not to stdout, which carries only the bench's JSON line
+            os.environ.setdefault("NCCL_DEBUG_FILE", os.path.join(tempfile.gettempdir(), f"vela_bench_nccl.{self.rank}.log"))
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", self.local))
             self.pg = True
