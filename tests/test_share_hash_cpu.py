@@ -83,3 +83,15 @@ def test_reference_digests(L, golden):
     for b in range(B):
         assert L.vela_share_hash(buf(g["headers"][b]), buf(g["poi"][b]), sh) == 0
         assert np.array_equal(np.frombuffer(sh.raw, np.uint8), g["share"][b])
+
+
+def test_python_helpers(golden):
+    """vela_b200.poi_out / poi_out_batch / share_hash / sha256d (the Python view of the same entry points)"""
+    g = golden("share_hash")
+    B = g["seeds"].shape[0]
+    assert V.poi_out(g["seeds"][0], g["x0"][0]) == g["poi"][0].tobytes()
+    assert V.poi_out_batch(g["seeds"], g["x0"], threads=2) == [g["poi"][b].tobytes() for b in range(B)]
+    assert V.share_hash(g["headers"][1], g["poi"][1]) == g["share"][1].tobytes()
+    assert V.sha256d(b"abc") == sha256(sha256(b"abc"))
+    with pytest.raises(ValueError):
+        V.poi_out(b"short", g["x0"][0])

@@ -46,6 +46,48 @@ def synth_model_write(path, seed=1):
     return path
 
 
+def _bytes_arg(b, n=None, what="buffer"):
+    b = bytes(memoryview(b).cast("B")) if not isinstance(b, (bytes, bytearray)) else bytes(b)
+    if n is not None and len(b) != n:
+        raise ValueError(f"{what}: {n} bytes expected, got {len(b)}")
+    return b
+
+
+def sha256d(data):
+    """SHA-256(SHA-256(data)) on the host (vela_sha256d)."""
+    d = _bytes_arg(data)
+    out = ctypes.create_string_buffer(32)
+    check(lib().vela_sha256d(d, len(d), out))
+    return out.raw
+
+
+def poi_out(seed, x0):
+    """The proof-of-inference hash of one inference: tagged SHA-256 "POI/out" over seed (32 bytes) and x0
+    (32768 bytes, int16 little-endian), as the reference's miner computes it (vela_poi_out)."""
+    out = ctypes.create_string_buffer(32)
+    check(lib().vela_poi_out(_bytes_arg(seed, 32, "seed"), _bytes_arg(x0, 32768, "x0"), out))
+    return out.raw
+
+
+def poi_out_batch(seeds, x0, threads=4):
+    """poi_out of every inference of a batch: seeds [batch][32] and x0 [batch][32768] (e.g. Engine.run's output),
+    hashed on up to `threads` host threads; returns a list of 32-byte digests."""
+    s, x = _bytes_arg(seeds), _bytes_arg(x0)
+    batch = len(s) // 32
+    if batch == 0 or len(s) != 32 * batch or len(x) != 32768 * batch:
+        raise ValueError("poi_out_batch: seeds must be batch x 32 bytes and x0 batch x 32768 bytes")
+    out = ctypes.create_string_buffer(32 * batch)
+    check(lib().vela_poi_out_batch(s, x, batch, int(threads), out))
+    return [out.raw[32 * b:32 * b + 32] for b in range(batch)]
+
+
+def share_hash(header80, poi32):
+    """The share hash sha256d(header[80] || poi[32]) the reference's miner compares with the pool target."""
+    out = ctypes.create_string_buffer(32)
+    check(lib().vela_share_hash(_bytes_arg(header80, 80, "header"), _bytes_arg(poi32, 32, "poi"), out))
+    return out.raw
+
+
 class Model:
     """Weights of one GPU (vela_model_load): a POISD file prepared for the tcgen05 kernels."""
 
