@@ -24,7 +24,10 @@ Our arm (--impl vela), one JSON line from rank 0:
 
 The reference arm (--impl reference) runs the reference engine itself, compiled from the reference's own
 sources (oracle/_ref/libvela_ref.so, built by `make -C oracle ref`), through its own Engine::submit /
-collect with one host thread per lane, on the same model file, batch, lanes and steps.
+collect with one host thread per lane, on the same model bytes, batch, lanes and steps.  Its process loads no
+library of the product: the model file comes from the test side's writer (oracle/synth_model.c), which gives the
+same bytes as vela_synth_model_write.  Its cpu_baseline is the oracle's CPU restatement (the reference has no CPU
+implementation of the path), the same bounded sample as our arm's.
 """
 import argparse
 import hashlib
@@ -165,12 +168,37 @@ class Clocks:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
-def model_file(rank):
-    import vela_b200 as V
-    path = os.path.join(tempfile.gettempdir(), f"vela_synth_seed{MODEL_SEED}_rank{rank}.poisd")
-    if not os.path.exists(path) or os.path.getsize(path) < (1 << 30):
-        V.synth_model_write(path, MODEL_SEED)
+def model_file(R, writer):
+    """The seeded synthetic model (~1.2 GB), written once per box and arm: rank 0 writes it to a temporary name and
+    renames it into place, the other ranks wait at a barrier, so N ranks share one file.  `writer` is "product"
+    (vela_synth_model_write, our arm) or "oracle" (the test side's writer, the reference arm, whose process must not
+    load the product library); both give the same bytes for the same seed (tests/test_synth_model_cpu.py)."""
+    path = os.path.join(tempfile.gettempdir(), f"vela_synth_seed{MODEL_SEED}_{writer}.poisd")
+    if R.rank == 0 and not (os.path.exists(path) and os.path.getsize(path) > (1 << 30)):
+        tmp = f"{path}.tmp{os.getpid()}"
+        if writer == "product":
+            import vela_b200 as V
+            V.synth_model_write(tmp, MODEL_SEED)
+        else:
+            from oracle import pyoracle as O
+            O.synth_model_write(tmp, MODEL_SEED)
+        os.replace(tmp, path)
+    R.barrier()
     return path
+
+
+def loaded_native_libs():
+    """shared libraries of this repository mapped into this process (from /proc/self/maps)"""
+    out = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                p = line.split()[-1] if line.strip() else ""
+                if p.endswith(".so") and p.startswith(ROOT):
+                    out.add(os.path.relpath(p, ROOT))
+    except OSError:
+        pass
+    return sorted(out)
 
 
 def peaks():
@@ -474,7 +502,7 @@ def run_vela(a, R):
     import vela_b200 as V
     from vela_b200.dist import seed_block, golden_seeds
     dev = torch.device("cuda", R.local)
-    path = model_file(R.rank)
+    path = model_file(R, "product")
     model = V.Model(path, R.local)
     lanes = [V.Engine(model, batch=a.batch, graph=True) for _ in range(a.lanes)]
     for e in lanes:
@@ -599,7 +627,7 @@ def run_reference(a, R):
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libvela_ref.so (the reference built from its sources) is missing; "
                                                                   "build it with `make -C oracle ref` where the reference checkout is present"}), flush=True)
         return
-    path = model_file(R.rank)
+    path = model_file(R, "oracle")
     L = ctypes.CDLL(so)
     L.ref_open.restype = ctypes.c_void_p
     L.ref_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
@@ -622,6 +650,9 @@ def run_reference(a, R):
     R.barrier()
     s = R.max(sec.value)
     L.ref_close(h)
+    # the CPU figure beside it: the reference has no CPU implementation of the path, so this is the oracle's C
+    # restatement of its integer spec (kind "port"), the same bounded sample as our arm's
+    cpu = cpu_baseline(path) if R.world == 1 and R.rank == 0 and not a.no_cpu_baseline else None
     if R.rank == 0:
         per_step = a.lanes * a.batch
         value = R.world * per_step * a.steps / s
@@ -632,10 +663,13 @@ def run_reference(a, R):
                                        "one CUDA graph per lane step", "batch": a.batch, "lanes": a.lanes, "inferences_per_step_per_gpu": per_step,
                            "prompt_tokens": PROMPT, "l2": "inputs larger than L2: 1.4 GB of weights and ~2 GB of activations stream per step"},
                 "impl": "reference",
-                "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": a.lanes, "kind": "reference",
-                                 "sample": f"the reference engine compiled from its own sources for sm_100 (oracle/_ref/libvela_ref.so): "
-                                           f"Engine::submit/collect from {a.lanes} host threads per GPU (src/main.cpp:111-162), "
-                                           f"{a.steps} steps per lane after {a.warmup} warm-up steps; it runs on the GPU, the host threads only drive it"},
+                "reference_kind": "gpu",
+                "reference_run": f"the reference engine compiled from its own sources for sm_100 (oracle/_ref/libvela_ref.so, cuBLASLt + "
+                                 f"mma.sync kernels, default EngineConfig): Engine::submit/collect from {a.lanes} host threads per GPU "
+                                 f"(src/main.cpp:111-162), {a.steps} steps per lane after {a.warmup} warm-up steps, on the same model bytes "
+                                 f"(written by oracle/synth_model.c), prompt, batch and lanes as our arm",
+                "cpu_baseline": cpu,
+                "native_libs": loaded_native_libs(),
                 "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": per_step * 32, "d2h_bytes_per_step": per_step * 32768},
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)

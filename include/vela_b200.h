@@ -82,6 +82,12 @@ typedef struct vela_aepi {
  * sources and all five epilogues; deep K included (the reference's cuBLASLt path, src/engine.cu:153-157). */
 int vela_gemm_w8a16(void* stream, const vela_asrc* A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
                     const int32_t* cst, const vela_aepi* E);
+/* Failure-path test entry (no reference counterpart; the reference's kernels have no bounded waits): the launch of
+ * vela_gemm_w8a16 with its TMA producers idle and every barrier wait limited to wait_limit_cycles SM clock cycles, so
+ * the waits run out, the kernel drains (nothing is in flight), frees its TMEM and returns; the timeout then reads
+ * as non-zero from vela_device_error.  Outputs are left unwritten. */
+int vela_gemm_w8a16_stalled(void* stream, const vela_asrc* A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                            const int32_t* cst, const vela_aepi* E, long long wait_limit_cycles);
 /* Planar form; replaces k_gemm_hl (src/gemm_hl.h:31-33). */
 int vela_gemm_hl(void* stream, const int8_t* Ahi, const int8_t* Alo, int lda, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
                  const int32_t* cst, const int32_t* e, int32_t* Y, int ldy, const int32_t* residual, int epi, int Cs, int32_t* Y1, int32_t* Y2,
@@ -155,6 +161,14 @@ int vela_fused_attention(void* stream, const int8_t* qhi, const int8_t* qlo, con
                          int B, int heads, int Tq, int Tqp, int Tk, int Tkp, int causal, const int32_t* lexp32, int C,
                          int32_t* gmx, int64_t* gr, int32_t* out, uint32_t* rowmax);
 
+/* Failure-path test entry (no reference counterpart): vela_fused_attention with its TMA producer idle and every
+ * wait limited to wait_limit_cycles SM clock cycles; the kernel drains and returns, vela_device_error reads non-zero. */
+int vela_fused_attention_stalled(void* stream, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, const int64_t* qhs, const int64_t* qls,
+                                 const int8_t* khi, const int8_t* klo, const int32_t* ek, const int64_t* ksum,
+                                 const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const int64_t* vsum,
+                                 int B, int heads, int Tq, int Tqp, int Tk, int Tkp, int causal, const int32_t* lexp32, int C,
+                                 int32_t* out, uint32_t* rowmax, long long wait_limit_cycles);
+
 /* ---------------------------------------------------------------------------------
  * Engine: one denoising step of the SD-turbo UNet per batch (src/engine.h:16-124).
  * A model holds the prepared weights of one GPU and is shared read-only by its engines; an engine
@@ -195,6 +209,10 @@ int vela_engine_step_taps(vela_engine* e, const uint8_t* seeds, uint8_t* x0, vel
 int vela_engine_launch_device(vela_engine* e, const uint8_t* d_seeds, uint8_t* d_x0);
 /* kernel nodes in the engine's last captured step graph (0 before the first capture; no reference counterpart) */
 int vela_engine_graph_kernels(const vela_engine* e);
+/* The engine's own device error word (its kernels report a timed-out bounded wait there; a step whose kernels did
+ * makes vela_engine_collect / vela_engine_run return VELA_ERR_TIMEOUT).  Synchronises the engine's stream;
+ * clear != 0 resets the word.  No reference counterpart (the reference's kernels have no bounded waits). */
+unsigned vela_engine_device_error(vela_engine* e, int clear);
 int vela_engine_in_flight(const vela_engine* e);
 int vela_engine_batch(const vela_engine* e);
 size_t vela_engine_arena_peak(const vela_engine* e);

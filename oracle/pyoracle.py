@@ -16,8 +16,8 @@ _lib = None
 
 def build():
     """Compile liboracle.so if missing or stale (gcc + OpenMP)."""
-    src = os.path.join(HERE, "vela_oracle.c")
-    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(src), os.path.getmtime(os.path.join(HERE, "vela_oracle.h"))):
+    srcs = [os.path.join(HERE, f) for f in ("vela_oracle.c", "vela_oracle.h", "synth_model.c")]
+    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
     return LIB_PATH
 
@@ -55,6 +55,7 @@ def lib():
                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.or_chacha20_block.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
         L.or_set_threads.argtypes = [ctypes.c_int]
+        L.or_synth_model_write.argtypes = [ctypes.c_char_p, ctypes.c_uint64]
         _lib = L
     return _lib
 
@@ -228,6 +229,15 @@ def attention(qhi, qlo, eq, khi, klo, ek, vhi, vlo, ev, B, heads, Tq, Tk, causal
     lib().or_attention(ptr(qhi), ptr(qlo), ptr(c32(eq)), Tqp, ptr(khi), ptr(klo), ptr(c32(ek)), ptr(vhi), ptr(vlo), ptr(c32(ev)),
                        B, heads, Tq, Tk, Tkp, int(causal), ptr(c32(lexp)), C, ptr(out), ptr(rm))
     return out, rm
+
+
+def synth_model_write(path, seed=1):
+    """the seeded random-init POISD model written by the test side (oracle/synth_model.c); the same bytes as the
+    product's vela_synth_model_write for the same seed"""
+    rc = lib().or_synth_model_write(path.encode(), int(seed))
+    if rc != 0:
+        raise RuntimeError(f"oracle model writer failed ({rc}) for {path}")
+    return path
 
 
 class Model:

@@ -121,6 +121,9 @@ int  or_unet_step(or_model_t* m, const uint8_t* seeds, int B, uint8_t* x0, int32
                   or_tap_fn tap, void* user);
 /* threads used by the OpenMP loops (0 = library default) */
 void or_set_threads(int n);
+/* Seeded random-init POISDv1 model (oracle/synth_model.c): the same bytes as the product's
+ * vela_synth_model_write for the same seed.  0 on success. */
+int or_synth_model_write(const char* path, uint64_t seed);
 int  or_get_threads(void);
 
 #ifdef __cplusplus

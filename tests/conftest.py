@@ -25,3 +25,12 @@ def golden():
             cache[name] = np.load(os.path.join(GOLDEN, name + ".npz"))
         return cache[name]
     return load
+
+
+@pytest.fixture(scope="session")
+def synth_model_path(tmp_path_factory):
+    """the seeded random-init POISD model of seed 1 (written once per session by the library's writer)"""
+    import vela_b200 as V
+    path = str(tmp_path_factory.mktemp("model") / "synth_seed1.poisd")
+    V.synth_model_write(path, 1)
+    return path

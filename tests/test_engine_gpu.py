@@ -24,10 +24,8 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 @pytest.fixture(scope="module")
-def model(tmp_path_factory):
-    path = str(tmp_path_factory.mktemp("model") / "synth.poisd")
-    V.synth_model_write(path, 1)
-    m = V.Model(path)
+def model(synth_model_path):
+    m = V.Model(synth_model_path)
     yield m
     m.close()
 

@@ -179,6 +179,10 @@ class Engine:
     def graph_kernels(self):
         return lib().vela_engine_graph_kernels(self.h)
 
+    def device_error(self, clear=True):
+        """the engine's device error word (non-zero: one of its kernels gave up a bounded wait); clear resets it"""
+        return lib().vela_engine_device_error(self.h, int(bool(clear)))
+
     @property
     def last_ms(self):
         return lib().vela_engine_last_ms(self.h)

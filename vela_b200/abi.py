@@ -40,6 +40,7 @@ SIGNATURES = {
     "vela_poi_out_batch": (I, [P, P, I, I, P]),
     "vela_share_hash": (I, [P, P, P]),
     "vela_gemm_w8a16": (I, [P, ctypes.POINTER(ASrc), I, I, P, I, I, I, I, P, ctypes.POINTER(AEpi)]),
+    "vela_gemm_w8a16_stalled": (I, [P, ctypes.POINTER(ASrc), I, I, P, I, I, I, I, P, ctypes.POINTER(AEpi), LL]),
     "vela_gemm_hl": (I, [P, P, P, I, I, I, P, I, I, I, I, P, P, P, I, P, I, I, P, P, P]),
     "vela_conv_e": (I, [P, P, I, I, I, I, P]),
     "vela_quant_rows": (I, [P, P, I, I, I, P, P, P, I]),
@@ -62,6 +63,7 @@ SIGNATURES = {
     "vela_quant_v": (I, [P, P, I, I, I, I, I, P, P, P, P, P]),
     "vela_quant_v_static": (I, [P, P, I, I, I, I, I, P, P, P, P]),
     "vela_fused_attention": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, P, P]),
+    "vela_fused_attention_stalled": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, LL]),
     "vela_model_load": (P, [I, ctypes.c_char_p]),
     "vela_model_free": (None, [P]),
     "vela_model_bytes": (SZ, [P]),
@@ -75,6 +77,7 @@ SIGNATURES = {
     "vela_engine_step_taps": (I, [P, P, P, P, P]),
     "vela_engine_launch_device": (I, [P, P, P]),
     "vela_engine_graph_kernels": (I, [P]),
+    "vela_engine_device_error": (U, [P, I]),
     "vela_engine_in_flight": (I, [P]),
     "vela_engine_batch": (I, [P]),
     "vela_engine_arena_peak": (SZ, [P]),

@@ -25,6 +25,7 @@
 #include "intops.cuh"
 #include "tc.cuh"
 #include "host_util.h"
+#include "ops.h"
 #include "vela_b200.h"
 #include <climits>
 #include <cstring>
@@ -66,6 +67,8 @@ struct AttnArgs {
     int32_t* out; uint32_t* rowmax;
     int heads, Tq, Tqp, Tk, Tkp, C, causal;
     unsigned* err;
+    long long wait_limit;          // SM clock cycles before a barrier wait gives up
+    int stall;                     // failure-path tests: the TMA producer issues nothing
 };
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -221,13 +224,13 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
 
     if (warp == 0) {
         // ---------------------------------------------------------------- producer
-        if (lane == 0) {
+        if (lane == 0 && !a.stall) {
             mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
             tma_load_2d(sm + OFF_Q, &a.tmQh, q_full, 0, g * a.Tqp + q0);
             tma_load_2d(sm + OFF_Q + Q_BYTES, &a.tmQl, q_full, 0, g * a.Tqp + q0);
             for (int it = 0; it < nIt; ++it) {
                 const int j = it % nT, ks = it % KS;
-                if (!mbar_wait(&k_empty[ks], ((it / KS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
+                if (!mbar_wait(&k_empty[ks], ((it / KS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) break;
                 uint8_t* kst = sm + OFF_K + ks * KSTAGE;
                 uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
                 mbar_arrive_expect_tx(&k_full[ks], KSTAGE + KAUX_BYTES);
@@ -237,7 +240,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 bulk_load(aux + 256, a.ksum + size_t(g) * a.Tkp + j * 64, 64 * 8, &k_full[ks]);
                 if (it >= 2 * nT) {
                     const int vs = j % VS;
-                    if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) break;
+                    if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) break;
                     mbar_arrive_expect_tx(&v_full[vs], VSTAGE);
                     uint8_t* vst = sm + OFF_V + vs * VSTAGE;
                     tma_load_2d(vst, &a.tmVh, &v_full[vs], j * 64, g * 64);
@@ -252,11 +255,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
             const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + Q_BYTES;
             const uint32_t ph = smem_u32(sm + OFF_P), pl = ph + P_BYTES;
             const uint32_t pv = tmem + 192;                   // A: [192,256), Y: [256,320), D: [320,384)
-            bool ok = mbar_wait(q_full, 0, a.err, DEVERR_TIMEOUT_FULL);
+            bool ok = mbar_wait(q_full, 0, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit);
             auto issue_pv = [&](int j) -> bool {
                 const int vs = j % VS;
-                if (!mbar_wait(p_full, j & 1, a.err, DEVERR_TIMEOUT_FULL)) return false;
-                if (!mbar_wait(&v_full[vs], (j / VS) & 1, a.err, DEVERR_TIMEOUT_FULL)) return false;
+                if (!mbar_wait(p_full, j & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) return false;
+                if (!mbar_wait(&v_full[vs], (j / VS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) return false;
                 tc_fence_after();
                 const uint32_t vh = smem_u32(sm + OFF_V + vs * VSTAGE), vl = vh + KT_BYTES;
                 #pragma unroll
@@ -277,10 +280,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 // earlier uses of buffer b: passes 0-1 alternate the buffers, pass 2 keeps buffer 0
                 const int ub = it < 2 * nT ? (it >> 1) : it - nT;
                 if (pass == 2 && j == 0) {      // the P.V accumulators reuse buffer 1's columns (used nT times)
-                    if (!mbar_wait(&qk_free[1], (nT & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    if (!mbar_wait(&qk_free[1], (nT & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) { ok = false; break; }
                 }
-                if (!mbar_wait(&k_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL)) { ok = false; break; }
-                if (!mbar_wait(&qk_free[b], (ub & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                if (!mbar_wait(&k_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) { ok = false; break; }
+                if (!mbar_wait(&qk_free[b], (ub & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t kh = smem_u32(sm + OFF_K + ks * KSTAGE), kl = kh + KT_BYTES;
                 const uint32_t d = tmem + b * 192;
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 const int it = pass * nT + j, ks = it % KS;
                 const int b = pass < 2 ? (it & 1) : 0;
                 const int ub = it < 2 * nT ? (it >> 1) : it - nT;      // earlier uses of buffer b
-                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL));
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
                 if (ok) {
                     tc_fence_after();
                     // this warp's 16 keys: exponent and 128 * ksum, staged once per tile for vector reads
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                     else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
                     else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
                     if (pass == 2) {
-                        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY));
+                        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit));
                         if (ok) {
                             uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
                             *reinterpret_cast<uint4*>(php + sw64_off(rl, kq)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
@@ -372,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         red[kq * 128 + rl] = psum;
         asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
         const i64 ps = red[rl] + red[128 + rl] + red[256 + rl] + red[384 + rl];
-        const bool done = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC));
+        const bool done = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC, a.wait_limit));
         tc_fence_after();
         if (done) {
             const int bidx = g / a.heads, h = g % a.heads;
@@ -410,7 +413,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
 void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, const i64* qhs, const i64* qls,
                      const int8_t* khi, const int8_t* klo, const int32_t* ek, const i64* ksum,
                      const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const i64* vsum,
-                     int B, int heads, int Tq, int Tqp, int Tk, int Tkp, bool causal, const int32_t* lexp, int C, int32_t* out, uint32_t* rowmax) {
+                     int B, int heads, int Tq, int Tqp, int Tk, int Tkp, bool causal, const int32_t* lexp, int C, int32_t* out, uint32_t* rowmax,
+                     const LaunchOpts& o) {
     VELA_REQUIRE(qhi && qlo && eq && qhs && qls && khi && klo && ek && ksum && vthi && vtlo && ev && vsum && lexp && out, "attention: null operand");
     VELA_REQUIRE(B > 0 && heads > 0 && C == heads * 64 && Tq > 0 && Tq <= Tqp && Tqp % 64 == 0 && Tk > 0 && Tk <= Tkp && Tkp % 64 == 0 && Tkp <= 4096,
                  "attention: needs C = 64*heads, Tqp % 64 == 0, Tkp % 64 == 0, Tk <= Tkp <= 4096");
@@ -426,13 +430,11 @@ void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, cons
     a.eq = eq; a.qhs = qhs; a.qls = qls; a.ek = ek; a.ksum = ksum; a.ev = ev; a.vsum = vsum; a.lexp = lexp;
     a.out = out; a.rowmax = rowmax;
     a.heads = heads; a.Tq = Tq; a.Tqp = Tqp; a.Tk = Tk; a.Tkp = Tkp; a.C = C; a.causal = causal ? 1 : 0;
-    a.err = device_error_word(&g_attn_err);
-    static int attr_done[64] = {0};
-    const int dev = current_device();
-    if (dev >= 64 || !attr_done[dev]) {
-        VELA_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        if (dev < 64) attr_done[dev] = 1;
-    }
+    a.err = o.err ? o.err : device_error_word(&g_attn_err);
+    a.wait_limit = o.wait_limit > 0 ? o.wait_limit : WAIT_LIMIT_CYCLES;
+    a.stall = o.stall;
+    static std::atomic<int> attr_done[64];
+    once_per_device(attr_done, [] { VELA_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)); });
     attn_kernel<<<dim3(ceil_div(Tqp, 128), G), THREADS, SMEM, st>>>(a);
     VELA_CUDA(cudaGetLastError());
 }
@@ -452,5 +454,20 @@ extern "C" int vela_fused_attention(void* stream, const int8_t* qhi, const int8_
     return guarded("vela_fused_attention", [&] {
         fused_attention(static_cast<cudaStream_t>(stream), qhi, qlo, eq, qhs, qls, khi, klo, ek, ksum, vthi, vtlo, ev, vsum,
                         B, heads, Tq, Tqp, Tk, Tkp, causal != 0, lexp32, C, out, rowmax);
+    });
+}
+// Failure-path test of the bounded waits (no reference counterpart): vela_fused_attention with the TMA producer idle
+// and a wait limit of wait_limit_cycles, so every wait of the MMA and softmax warps runs out; the kernel drains, frees
+// its TMEM and returns, and vela_device_error reports the timeout.  Nothing is in flight when the waits give up.
+extern "C" int vela_fused_attention_stalled(void* stream, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, const int64_t* qhs, const int64_t* qls,
+                                            const int8_t* khi, const int8_t* klo, const int32_t* ek, const int64_t* ksum,
+                                            const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const int64_t* vsum,
+                                            int B, int heads, int Tq, int Tqp, int Tk, int Tkp, int causal, const int32_t* lexp32, int C,
+                                            int32_t* out, uint32_t* rowmax, long long wait_limit_cycles) {
+    return guarded("vela_fused_attention_stalled", [&] {
+        VELA_REQUIRE(wait_limit_cycles > 0, "non-positive wait limit");
+        LaunchOpts o; o.wait_limit = wait_limit_cycles; o.stall = 1;
+        fused_attention(static_cast<cudaStream_t>(stream), qhi, qlo, eq, qhs, qls, khi, klo, ek, ksum, vthi, vtlo, ev, vsum,
+                        B, heads, Tq, Tqp, Tk, Tkp, causal != 0, lexp32, C, out, rowmax, o);
     });
 }

@@ -233,12 +233,27 @@ public:
         dEps_ = static_cast<int32_t*>(palloc(size_t(B_) * 16384 * 4)); dIds_ = static_cast<int32_t*>(palloc(128 * 4));
         dCtx_ = static_cast<int32_t*>(palloc(size_t(77) * m.te_dim * 4));
         VELA_CUDA(cudaEventCreate(&ev0_)); VELA_CUDA(cudaEventCreateWithFlags(&ev1_, cudaEventBlockingSync));
+        // this engine's own device error word: its kernels report a timed-out wait here, and each step copies it out
+        // beside x0, so collect / run fail with VELA_ERR_TIMEOUT for exactly the steps that timed out
+        dErr_ = static_cast<unsigned*>(palloc(sizeof(unsigned)));
+        VELA_CUDA(cudaMemset(dErr_, 0, sizeof(unsigned)));
+        for (int s = 0; s < 2; ++s) {
+            VELA_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&hErr_[s]), sizeof(unsigned), cudaHostAllocDefault));
+            *hErr_[s] = 0;
+        }
+        lo_.err = dErr_;
     }
     ~Engine() {
         cudaSetDevice(m_.device);
         if (st_) cudaStreamSynchronize(st_);
         if (gexec_dev_) cudaGraphExecDestroy(gexec_dev_);
-        for (int s = 0; s < 2; ++s) { if (gexec_[s]) cudaGraphExecDestroy(gexec_[s]); if (done_[s]) cudaEventDestroy(done_[s]); if (hSeeds_[s]) cudaFreeHost(hSeeds_[s]); if (hOut_[s]) cudaFreeHost(hOut_[s]); }
+        for (int s = 0; s < 2; ++s) {
+            if (gexec_[s]) cudaGraphExecDestroy(gexec_[s]);
+            if (done_[s]) cudaEventDestroy(done_[s]);
+            if (hSeeds_[s]) cudaFreeHost(hSeeds_[s]);
+            if (hOut_[s]) cudaFreeHost(hOut_[s]);
+            if (hErr_[s]) cudaFreeHost(hErr_[s]);
+        }
         for (void* p : persist_) cudaFree(p);
         if (ev0_) cudaEventDestroy(ev0_); if (ev1_) cudaEventDestroy(ev1_);
         if (st_) cudaStreamDestroy(st_);
@@ -297,6 +312,8 @@ public:
         }
         VELA_CUDA(cudaStreamSynchronize(st_));
         VELA_CUDA(cudaGetLastError());
+        if (const unsigned v = device_error(true))
+            throw Error(VELA_ERR_TIMEOUT, "a kernel of the text encoder gave up a bounded wait (device error code " + std::to_string(v) + ")");
         have_prompt_ = true;
     }
     void context(int32_t* host) {
@@ -317,6 +334,7 @@ public:
         VELA_CUDA(cudaEventSynchronize(ev1_));
         VELA_CUDA(cudaGetLastError());
         float ms = 0; VELA_CUDA(cudaEventElapsedTime(&ms, ev0_, ev1_)); last_ms = ms;
+        check_step(0);
         std::memcpy(x0, hOut_[0], size_t(32768) * B_);
     }
     // ---- pipelined form: two batches in flight, each with its own I/O buffers and graph (src/engine.cu:610-649)
@@ -336,8 +354,9 @@ public:
         const int slot = col_slot_;
         VELA_CUDA(cudaEventSynchronize(done_[slot]));
         VELA_CUDA(cudaGetLastError());
-        std::memcpy(x0, hOut_[slot], size_t(32768) * B_);
         col_slot_ ^= 1; --inflight_;
+        check_step(slot);
+        std::memcpy(x0, hOut_[slot], size_t(32768) * B_);
     }
     // ---- device-resident form: seeds and x0 in device memory, enqueued on st_ without waiting (slot 0's buffers)
     void launch_device(const uint8_t* dseeds, uint8_t* dx0) {
@@ -351,6 +370,15 @@ public:
         VELA_CUDA(cudaMemcpyAsync(dx0, dOut_[0], size_t(32768) * B_, cudaMemcpyDeviceToDevice, st_));
     }
     int graph_kernels() const { return graph_kernels_; }
+    // the engine's device error word (synchronises the engine's stream); clear: reset it to zero
+    unsigned device_error(bool clear) {
+        VELA_CUDA(cudaSetDevice(m_.device));
+        VELA_CUDA(cudaStreamSynchronize(st_));
+        unsigned v = 0;
+        VELA_CUDA(cudaMemcpy(&v, dErr_, sizeof(v), cudaMemcpyDeviceToHost));
+        if (clear && v) VELA_CUDA(cudaMemset(dErr_, 0, sizeof(unsigned)));
+        return v;
+    }
     // ---- one eager step with every block output handed to `tap` (parity against the reference's blocks)
     void step_taps(const uint8_t* seeds, uint8_t* x0, TapFn tap, void* user) {
         VELA_REQUIRE(have_prompt_, "step_taps: no prompt set");
@@ -362,6 +390,7 @@ public:
         tap_ = nullptr;
         VELA_CUDA(cudaStreamSynchronize(st_));
         VELA_CUDA(cudaGetLastError());
+        check_step(0);
         std::memcpy(x0, hOut_[0], size_t(32768) * B_);
     }
 
@@ -374,6 +403,7 @@ private:
     cudaEvent_t done_[2] = {nullptr, nullptr}, ev0_ = nullptr, ev1_ = nullptr;
     int inflight_ = 0, sub_slot_ = 0, col_slot_ = 0;
     int32_t *dNoise_ = nullptr, *dX_ = nullptr, *dEps_ = nullptr, *dIds_ = nullptr, *dCtx_ = nullptr;
+    unsigned* dErr_ = nullptr; unsigned* hErr_[2] = {nullptr, nullptr}; LaunchOpts lo_;
     KV cross_[16];
     bool have_prompt_ = false;
     TapFn tap_ = nullptr; void* tap_user_ = nullptr;
@@ -415,7 +445,7 @@ private:
         VELA_REQUIRE(q.K == L.K && q.Kp == L.Kp, "lin_q: K mismatch");
         Tensor y; y.B = q.B; y.T = q.T; y.C = L.N; y.d = out ? out : static_cast<int32_t*>(arena_.alloc(y.n() * 4)); y.rowmax = rowmax;
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = q.hi; A.lo = q.lo; A.ld8 = q.Kp; A.e = q.e;
-        gemm_w8a16(st_, A, q.Mp, q.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, rowmax));
+        gemm_w8a16(st_, A, q.Mp, q.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, rowmax), lo_);
         return y;
     }
     // int32 input quantised on load (Engine::linX, src/engine.cu:162-175); the row max comes from the producer or a pixmax pass
@@ -439,11 +469,11 @@ private:
             int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
             quant_rows_rm(st_, xd, rm, rows, K, K, hi, lo, e, L.Kp, Mp);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;
-            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
+            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
             return;
         }
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_X32; A.x = xd; A.ldx = K; A.rowmax = rm; A.K = L.K;
-        gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
+        gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
     }
     // 3x3 pad-1 convolution (Engine::conv3, src/engine.cu:254-280): implicit GEMM on the int32 image
     Tensor conv3(const Tensor& x, int H, int W, const Lin& L, int stride, int32_t* out = nullptr, const int32_t* residual = nullptr, const uint32_t* pmIn = nullptr) {
@@ -458,14 +488,14 @@ private:
             int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
             conv_e(st_, pm, x.B, H, W, stride, e);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_CONV32; A.img = x.d; A.H = H; A.W = W; A.C = x.C; A.stride = stride; A.Ho = Ho; A.Wo = Wo; A.K = L.K; A.e = e;
-            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr));
+            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
         } else {       // 4-channel input image: explicit im2col (K = 36) then the planar GEMM
             const int Mp = int(align_up(rows, 32));
             int8_t* hi = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp)); int8_t* lo = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp));
             int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
             im2col3(st_, x.d, pm, x.B, H, W, x.C, stride, hi, lo, e, L.Kp);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;
-            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr));
+            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
         }
         arena_.off = mk;
         return y;
@@ -512,7 +542,7 @@ private:
         E.qhi = q.hi; E.qlo = q.lo; E.qe = q.e; E.qhs = q.hs; E.qls = q.ls; E.qts = q.ts;
         E.khi = k.hi; E.klo = k.lo; E.ke = k.e; E.khs = k.hs; E.kls = k.ls; E.kts = k.ts;
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n.hi; A.lo = n.lo; A.ld8 = n.Kp; A.e = n.e;
-        gemm_w8a16(st_, A, n.Mp, n.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
+        gemm_w8a16(st_, A, n.Mp, n.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
         if (TpQ > T) quant_heads(st_, nullptr, n.B, T, C, heads, TpQ, q.hi, q.lo, q.e, q.hs, q.ls, q.ts, T);
         if (TpK > T) quant_heads(st_, nullptr, n.B, T, C, heads, TpK, k.hi, k.lo, k.e, k.hs, k.ls, k.ts, T);
     }
@@ -525,7 +555,7 @@ private:
         E.epi = VELA_EPI_QKV; E.heads = heads; E.T = T; E.TpQ = TpQ; E.TpK = TpQ; E.C = C;
         E.qhi = q.hi; E.qlo = q.lo; E.qe = q.e; E.qhs = q.hs; E.qls = q.ls; E.qts = q.ts;
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n.hi; A.lo = n.lo; A.ld8 = n.Kp; A.e = n.e;
-        gemm_w8a16(st_, A, n.Mp, n.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E);
+        gemm_w8a16(st_, A, n.Mp, n.rows(), L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
         if (TpQ > T) quant_heads(st_, nullptr, n.B, T, C, heads, TpQ, q.hi, q.lo, q.e, q.hs, q.ls, q.ts, T);
         return q;
     }
@@ -543,7 +573,7 @@ private:
         Tensor out = talloc(q.B, Tq, C);
         out.rowmax = rowmax_alloc(q.B * Tq);
         fused_attention(st_, q.hi, q.lo, q.e, q.hs, q.ls, kv.khi, kv.klo, kv.ek, kv.ksum, kv.vhi, kv.vlo, kv.ev, kv.vsum,
-                        q.B, heads, Tq, q.Tp, kv.Tk, kv.Tkp, causal, m_.lut_exp, C, out.d, out.rowmax);
+                        q.B, heads, Tq, q.Tp, kv.Tk, kv.Tkp, causal, m_.lut_exp, C, out.d, out.rowmax, lo_);
         return out;
     }
     // Engine::resnet (src/engine.cu:389-405)
@@ -595,7 +625,7 @@ private:
             Tensor v; v.B = B; v.T = T; v.C = F; v.d = static_cast<int32_t*>(arena_.alloc(v.n() * 4)); v.rowmax = rowmax_alloc(B * T);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n.hi; A.lo = n.lo; A.ld8 = n.Kp; A.e = n.e;
             vela_aepi E; std::memset(&E, 0, sizeof(E)); E.epi = VELA_EPI_GEGLU; E.Y = v.d; E.ldy = F; E.Lphi = m_.lut_phi; E.rowmax = v.rowmax;
-            gemm_w8a16(st_, A, n.Mp, n.rows(), Li.w, Li.Kp, Li.Np, Li.N, Li.Kp, Li.cst, E);
+            gemm_w8a16(st_, A, n.Mp, n.rows(), Li.w, Li.Kp, Li.Np, Li.N, Li.Kp, Li.cst, E, lo_);
             const Lin& L2 = m_.lin(b + ".ff.net.2");
             VELA_REQUIRE(L2.K == F, "ff.net.2: K mismatch");
             gemm_x(v.d, B * T, F, v.rowmax, L2, epi_plain(h.d, C, h.d, h.rowmax));
@@ -671,7 +701,7 @@ private:
             Tensor f; f.B = 1; f.T = T; f.C = L1.N; f.d = static_cast<int32_t*>(arena_.alloc(f.n() * 4)); f.rowmax = rowmax_alloc(T);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n2.hi; A.lo = n2.lo; A.ld8 = n2.Kp; A.e = n2.e;
             vela_aepi E = epi_plain(f.d, L1.N, nullptr, f.rowmax); E.epi = VELA_EPI_GELU; E.Lphi = m_.lut_phi;
-            gemm_w8a16(st_, A, n2.Mp, T, L1.w, L1.Kp, L1.Np, L1.N, L1.Kp, L1.cst, E);
+            gemm_w8a16(st_, A, n2.Mp, T, L1.w, L1.Kp, L1.Np, L1.N, L1.Kp, L1.cst, E, lo_);
             lin_x(f, m_.lin(p + ".mlp.fc2"), x.d, x.d);
             arena_.off = mk;
         }
@@ -690,7 +720,19 @@ private:
         Tensor eps; eps.d = dEps_; eps.B = B_; eps.T = 4096; eps.C = 4;
         unet(x, eps);
         finalize(st_, dNoise_, dEps_, B_, m_.c_sig, dOut_[slot]);
-        if (io) VELA_CUDA(cudaMemcpyAsync(hOut_[slot], dOut_[slot], size_t(32768) * B_, cudaMemcpyDeviceToHost, st_));
+        if (io) {
+            VELA_CUDA(cudaMemcpyAsync(hOut_[slot], dOut_[slot], size_t(32768) * B_, cudaMemcpyDeviceToHost, st_));
+            VELA_CUDA(cudaMemcpyAsync(hErr_[slot], dErr_, sizeof(unsigned), cudaMemcpyDeviceToHost, st_));
+        }
+    }
+    // a finished step of `slot` whose kernels reported a timed-out wait: reset the word and fail (x0 is not valid)
+    void check_step(int slot) {
+        const unsigned v = *hErr_[slot];
+        if (!v) return;
+        *hErr_[slot] = 0;
+        VELA_CUDA(cudaMemsetAsync(dErr_, 0, sizeof(unsigned), st_));
+        VELA_CUDA(cudaStreamSynchronize(st_));
+        throw Error(VELA_ERR_TIMEOUT, "a kernel of the step gave up a bounded wait (device error code " + std::to_string(v) + ")");
     }
     cudaGraphExec_t capture(int slot, bool io) {
         forward(slot, io);
@@ -774,6 +816,10 @@ extern "C" int vela_engine_launch_device(vela_engine* e, const uint8_t* d_seeds,
     return guarded("vela_engine_launch_device", [&] { VELA_REQUIRE(e && d_seeds && d_x0, "bad arguments"); e->e->launch_device(d_seeds, d_x0); });
 }
 extern "C" int vela_engine_graph_kernels(const vela_engine* e) { return e ? e->e->graph_kernels() : 0; }
+extern "C" unsigned vela_engine_device_error(vela_engine* e, int clear) {
+    if (!e) return 0;
+    try { return e->e->device_error(clear != 0); } catch (...) { return 0xFFFFFFFFu; }
+}
 extern "C" int vela_engine_in_flight(const vela_engine* e) { return e ? e->e->in_flight() : 0; }
 extern "C" int vela_engine_batch(const vela_engine* e) { return e ? e->e->batch() : 0; }
 extern "C" size_t vela_engine_arena_peak(const vela_engine* e) { return e ? e->e->arena_peak() : 0; }

@@ -4,6 +4,7 @@
 #include "gemm_kernel.cuh"
 #include "gemm_persist.cuh"
 #include "host_util.h"
+#include "ops.h"
 #include "vela_b200.h"
 #include <algorithm>
 #include <cstdlib>
@@ -96,7 +97,7 @@ Plan plan(int src, int epi, int Mp, int Mreal, int Np, int Nreal, int nkb, size_
 }  // namespace
 
 void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
-                const int32_t* cst, const vela_aepi& E) {
+                const int32_t* cst, const vela_aepi& E, const LaunchOpts& o) {
     VELA_REQUIRE(Mp > 0 && Mreal > 0 && Mreal <= Mp && Nreal > 0 && Nreal <= Np && Kp > 0, "gemm: bad M/N/K");
     VELA_REQUIRE(Kp % 16 == 0 && ldw % 16 == 0 && ldw >= Kp && Np % 16 == 0, "gemm: Kp, ldw and Np must be multiples of 16");
     VELA_REQUIRE(W && cst, "gemm: null weights");
@@ -113,7 +114,9 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
     a.heads = E.heads; a.T = E.T; a.TpQ = E.TpQ; a.TpK = E.TpK; a.Cq = E.C;
     a.qhi = E.qhi; a.qlo = E.qlo; a.khi = E.khi; a.klo = E.klo; a.qe = E.qe; a.ke = E.ke;
     a.qhs = E.qhs; a.qls = E.qls; a.qts = E.qts; a.khs = E.khs; a.kls = E.kls; a.kts = E.kts;
-    a.err = device_error_word(&g_gemm_err);
+    a.err = o.err ? o.err : device_error_word(&g_gemm_err);
+    a.wait_limit = o.wait_limit > 0 ? o.wait_limit : WAIT_LIMIT_CYCLES;
+    a.stall = o.stall;
     const int epi = E.epi == VELA_EPI_GELU ? EPI_PLAIN : E.epi;
     VELA_REQUIRE(epi >= 0 && epi <= EPI_QKV, "gemm: unknown epilogue");
     if (epi == EPI_PLAIN) VELA_REQUIRE(E.Y && E.ldy >= Nreal, "gemm: plain epilogue needs Y and ldy >= N");
@@ -219,6 +222,17 @@ extern "C" int vela_gemm_w8a16(void* stream, const vela_asrc* A, int Mp, int Mre
     return guarded("vela_gemm_w8a16", [&] {
         VELA_REQUIRE(A && E, "null descriptor");
         gemm_w8a16(static_cast<cudaStream_t>(stream), *A, Mp, Mreal, W, ldw, Np, Nreal, Kp, cst, *E);
+    });
+}
+// Failure-path test of the bounded waits: the same launch with the TMA producers idle and a wait limit of
+// wait_limit_cycles, so every consumer's wait runs out, the kernel drains and returns and the timeout is reported in
+// the device error word (vela_device_error).  Nothing is in flight when the waits give up.
+extern "C" int vela_gemm_w8a16_stalled(void* stream, const vela_asrc* A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
+                                       const int32_t* cst, const vela_aepi* E, long long wait_limit_cycles) {
+    return guarded("vela_gemm_w8a16_stalled", [&] {
+        VELA_REQUIRE(A && E && wait_limit_cycles > 0, "null descriptor or non-positive wait limit");
+        LaunchOpts o; o.wait_limit = wait_limit_cycles; o.stall = 1;
+        gemm_w8a16(static_cast<cudaStream_t>(stream), *A, Mp, Mreal, W, ldw, Np, Nreal, Kp, cst, *E, o);
     });
 }
 extern "C" int vela_gemm_hl(void* stream, const int8_t* Ahi, const int8_t* Alo, int lda, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,

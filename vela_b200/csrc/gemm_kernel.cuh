@@ -41,6 +41,8 @@ struct GemmArgs {
     CUtensorMap tmY;                                        // plain epilogue with ytma = 1: Y [Mreal][Nreal] int32, box 16 x 32, 64B swizzle
     int ytma;
     unsigned* err;
+    long long wait_limit;                                   // SM clock cycles before a barrier wait gives up
+    int stall;                                              // failure-path tests: the TMA producers issue nothing
 };
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }

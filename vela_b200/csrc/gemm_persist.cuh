@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
+        if (lane == 0 && !a.stall) {
             int g = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int k = (kb0 + i) * Cfg::BK;
                     const int s = g % STAGES;
-                    if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) { ok = false; break; }
                     uint8_t* st = smem + s * Cfg::STAGE;
                     mbar_arrive_expect_tx(&full[s], Cfg::W_BYTES + (SRC == SRC_I8 ? 2 * Cfg::A_BYTES : 0));
                     tma_load_2d(st + 2 * Cfg::A_BYTES, &a.tmW, &full[s], k, n0);
@@ -132,13 +132,13 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tl) {
                 const int b = Cfg::ACC_BUFS == 2 ? (tl & 1) : 0, u = Cfg::ACC_BUFS == 2 ? (tl >> 1) : tl;
-                if (!mbar_wait(&acce[b], (u & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                if (!mbar_wait(&acce[b], (u & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(b * Cfg::ACC_COLS);
                 const int z = t / nMN, kb0 = z * kbs, nk = min(a.nkb, kb0 + kbs) - kb0;
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int s = g % STAGES;
-                    if (!mbar_wait(&full[s], (g / STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL)) { ok = false; break; }
+                    if (!mbar_wait(&full[s], (g / STAGES) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * Cfg::STAGE);
                     #pragma unroll
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
         }
     } else if (REG && warp == Cfg::X_WARP) {
         // ------------------------------------------------------------ int32 staging TMA (runs ahead of the W ring)
-        if (lane == 0 && a.xtma) {
+        if (lane == 0 && a.xtma && !a.stall) {
             int g = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 for (int i = 0; i < nk; ++i, ++g) {
                     const int k = (kb0 + i) * Cfg::BK;
                     const int xs = g % Cfg::XR;
-                    if (!mbar_wait(&xempty[xs], ((g / Cfg::XR) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    if (!mbar_wait(&xempty[xs], ((g / Cfg::XR) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) { ok = false; break; }
                     mbar_arrive_expect_tx(&xfull[xs], Cfg::X_STAGE);
                     #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                 int4 v[8];
                 const int xs = g % Cfg::XR;
                 if (a.xtma) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::XR) & 1, a.err, DEVERR_TIMEOUT_FULL))) { ok = false; break; }
+                    if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xs], (g / Cfg::XR) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit))) { ok = false; break; }
                     const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
                     #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                     }
                 }
                 const int s = g % STAGES;
-                if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY))) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit))) { ok = false; break; }
                 uint8_t* st = smem + s * Cfg::STAGE;
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                 *reinterpret_cast<uint4*>(st + sw64_off(row, half * 2 + 1)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             for (int i = lane; i < BN; i += 32) { const int4 cv = cb[i]; smin = min(smin, cv.y); smax = max(smax, cv.y); mbig |= uabs(cv.x) >> 23; }
             smin = __reduce_min_sync(0xffffffffu, smin); smax = __reduce_max_sync(0xffffffffu, smax);
             const bool fast = a.partial == nullptr && __all_sync(0xffffffffu, smin - er >= 1 && smax - er <= 31 && mbig == 0);
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC));
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC, a.wait_limit));
             if (!ok) continue;
             tc_fence_after();
             gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast, yb);
@@ -307,12 +307,8 @@ template <int BN, int STAGES, int SRC, int EPI>
 void launch_gemm_persist(const GemmArgs& a, cudaStream_t st) {
     using Cfg = PersistCfg<BN, STAGES, SRC, EPI>;
     auto kern = gemm_persist_kernel<BN, STAGES, SRC, EPI>;
-    static int attr_done[64] = {0};
-    const int dev = current_device();
-    if (dev >= 64 || !attr_done[dev]) {
-        VELA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-        if (dev < 64) attr_done[dev] = 1;
-    }
+    static std::atomic<int> attr_done[64];
+    once_per_device(attr_done, [&] { VELA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM)); });
     VELA_REQUIRE(a.kb_per_split > 0 && (a.partial != nullptr) == (a.kb_per_split < a.nkb) && (EPI == EPI_PLAIN || a.partial == nullptr),
                  "gemm: split-K needs a workspace and the plain epilogue");
     const int tiles = ceil_div(a.Np, BN) * ceil_div(a.Mp, 128) * ceil_div(a.nkb, a.kb_per_split);

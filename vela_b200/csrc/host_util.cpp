@@ -59,11 +59,11 @@ CUtensorMap tmap_nhwc(const void* base, uint64_t B, uint64_t H, uint64_t W, uint
 
 int current_device() { int d = 0; VELA_CUDA(cudaGetDevice(&d)); return d; }
 int sm_count() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];
     const int d = current_device();
-    if (d < 64 && cache[d]) return cache[d];
+    if (d < 64) { const int c = cache[d].load(std::memory_order_relaxed); if (c) return c; }
     int n = 0; VELA_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d));
-    if (d < 64) cache[d] = n;
+    if (d < 64) cache[d].store(n, std::memory_order_relaxed);
     return n;
 }
 

@@ -4,6 +4,7 @@
 #include "status.h"
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <cstddef>
 
@@ -29,4 +30,21 @@ void register_error_word(const void* symbol);
 
 int current_device();
 int sm_count();
+
+// Per-launch options of the kernels with bounded waits (GEMM, attention).
+struct LaunchOpts {
+    unsigned* err = nullptr;       // device error word the kernel reports a timeout into; null: the kernel file's own word
+    long long wait_limit = 0;      // SM clock cycles before a wait gives up; 0: the default (WAIT_LIMIT_CYCLES)
+    int stall = 0;                 // failure-path tests only: the TMA producers issue nothing, so every wait runs out
+};
+
+// Runs `f` (an idempotent per-device setup such as cudaFuncSetAttribute) until it has succeeded once on the current
+// device; `done` is a zero-initialised static array of 64 flags owned by the caller.  Threads may race into `f`
+// together, which is harmless for idempotent setups; the flags themselves are atomic.
+template <class F> void once_per_device(std::atomic<int>* done, F&& f) {
+    const int d = current_device();
+    if (d < 64 && done[d].load(std::memory_order_acquire)) return;
+    f();
+    if (d < 64) done[d].store(1, std::memory_order_release);
+}
 }  // namespace vela

@@ -2,6 +2,7 @@
 // All throw vela::Error on bad arguments; none synchronises or allocates.
 #pragma once
 #include "vela_b200.h"
+#include "host_util.h"
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -9,7 +10,7 @@
 namespace vela {
 typedef int64_t i64;
 void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const int8_t* W, int ldw, int Np, int Nreal, int Kp,
-                const int32_t* cst, const vela_aepi& E);
+                const int32_t* cst, const vela_aepi& E, const LaunchOpts& o = LaunchOpts());
 void conv_e(cudaStream_t st, const uint32_t* pm, int B, int H, int W, int stride, int32_t* e);
 void quant_rows(cudaStream_t st, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
 // quant_rows with the row maxima given (row_exp(rowmax[r]) = the row's exponent); rows [M, Mpad) zero-valued
@@ -34,5 +35,6 @@ void quant_v(cudaStream_t st, const int32_t* X, int B, int Tk, int C, int heads,
 void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, const i64* qhs, const i64* qls,
                      const int8_t* khi, const int8_t* klo, const int32_t* ek, const i64* ksum,
                      const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const i64* vsum,
-                     int B, int heads, int Tq, int Tqp, int Tk, int Tkp, bool causal, const int32_t* lexp, int C, int32_t* out, uint32_t* rowmax);
+                     int B, int heads, int Tq, int Tqp, int Tk, int Tkp, bool causal, const int32_t* lexp, int C, int32_t* out, uint32_t* rowmax,
+                     const LaunchOpts& o = LaunchOpts());
 }  // namespace vela

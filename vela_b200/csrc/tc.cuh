@@ -11,8 +11,15 @@ namespace vela {
 // Error word codes: a kernel whose bounded wait gives up writes one (first writer wins) into the error word
 // it was given (a __device__ variable of its translation unit), read by vela_device_error().
 enum : unsigned { DEVERR_NONE = 0, DEVERR_TIMEOUT_FULL = 1, DEVERR_TIMEOUT_EMPTY = 2, DEVERR_TIMEOUT_ACC = 3, DEVERR_TIMEOUT_OTHER = 4 };
-// A wait on a barrier gives up after this many SM clock cycles (~1.5 s at 1.9 GHz).
+// A wait on a barrier gives up after this many SM clock cycles (~1.5 s at 1.9 GHz) unless the launch passes a
+// shorter limit (the failure-path tests do).
 constexpr long long WAIT_LIMIT_CYCLES = 3000000000ll;
+// Suspend-time hint of a barrier probe in nanoseconds: a waiting warp is parked by the hardware until the phase
+// completes or the hint expires instead of re-issuing the probe, so waiting producer / MMA / epilogue warps leave the
+// issue slots to the warps doing arithmetic.
+#ifndef VELA_WAIT_HINT_NS
+#define VELA_WAIT_HINT_NS 0
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
 
@@ -28,16 +35,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
+#if VELA_WAIT_HINT_NS > 0
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "n"(VELA_WAIT_HINT_NS) : "memory");
+#else
     asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+#endif
     return ok != 0;
 }
-// Wait for the phase with the given parity to complete; false (and the device error word set) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err, unsigned errcode) {
+// Wait for the phase with the given parity to complete; false (and the device error word set) once `limit` SM clock
+// cycles have passed without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err, unsigned errcode, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicCAS(err, 0u, errcode); return false; }
+        if (clock64() - t0 > limit) { atomicCAS(err, 0u, errcode); return false; }
     }
     return true;
 }
