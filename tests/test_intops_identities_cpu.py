@@ -11,7 +11,9 @@ kernel computes and checks it against the spec form on edge values and seeded ra
 - lut_act_s: x * lut / 2^16 rounded needs no saturation when 0 <= lut <= 65536;
 - norm_val (rowops.cu): the binary64 quotient formed with the 1.5 * 2^52 constant and one fma residual test
   ==  floor((d 2^(25-e) + sd) / (2 sd));
-- the int32 staging quantiser and the attention score identities are covered by the GPU parity tests.
+- the attention softmax forms (attn.cu): the 32-bit score (hh M + mul.hi(T, 2^(32-a))) >> b, its mixed-exponent
+  variant, the exp table interpolated with one mad.hi, and P from the reciprocal's 32-bit halves;
+- the int32 staging quantiser is covered by the GPU parity tests.
 """
 import random
 import struct
@@ -171,3 +173,121 @@ def test_norm_quotient():
         sd = rnd.randint(max(1, -(-abs(d) * (1 << (25 - e)) // (1 << 30))), 1 << 28)
         want = (d * (1 << (25 - e)) + sd) // (2 * sd)
         assert norm_quotient_kernel(x, mean, e, sd) == want, (x, mean, e, sd)
+
+
+# ---------------------------------------------------------------- attention softmax (attn.cu)
+def s32(v):                 # two's-complement wrap to int32
+    v &= 0xFFFFFFFF
+    return v - (1 << 32) if v >= 1 << 31 else v
+
+
+def mulhi32(a, b):          # mul.hi.s32 of two int32 values
+    return (a * b) >> 32
+
+
+def div_pow2_model(hh, T, sh):
+    """attn.cu div_pow2 then >> b, for a = min(sh, 16), b = sh - a, M = 2^(16-a), A = 2^(32-a):
+    (hh M + mul.hi(T, A)) mod 2^32, then >> b"""
+    a = min(sh, 16)
+    assert 0 < (1 << (32 - a)) < 2**31
+    return s32(hh * (1 << (16 - a)) + mulhi32(T, 1 << (32 - a))) >> (sh - a)
+
+
+def _score_operands(rnd, n):
+    """(hh, xx, ll, kc, cq, S) drawn like the accumulators of a 64-dim head of 16-bit values (edges included)"""
+    out = []
+    for _ in range(n):
+        q = [rnd.choice([-32767, 32767, rnd.randint(-32767, 32767)]) for _ in range(64)]
+        k = [rnd.choice([-32767, 32767, rnd.randint(-32767, 32767)]) for _ in range(64)]
+        qh, ql = zip(*(planes(v) for v in q))
+        kh, kl = zip(*(planes(v) for v in k))
+        hh = sum(a * b for a, b in zip(qh, kh))
+        xx = sum(a * b for a, b in zip(qh, kl)) + sum(a * b for a, b in zip(ql, kh))
+        ll = sum(a * b for a, b in zip(ql, kl))
+        cq = 32768 * sum(qh) + 128 * sum(ql)
+        kc = 128 * sum(k)
+        S = sum(a * b for a, b in zip(q, k))
+        assert S == 65536 * hh + 256 * xx + ll + cq + kc
+        out.append((hh, xx, ll, kc, cq, S))
+    return out
+
+
+def test_attention_score_32bit_form():
+    """one key exponent per chunk: (hh M + mul.hi(T, 2^(32-a))) >> b == rshr(S, sh) for every shift the fast path takes"""
+    rnd = random.Random(21)
+    ops = _score_operands(rnd, 300)
+    ops.append((64 * 128 * 128, 0, 0, 0, 0, 64 * 128 * 128 * 65536))      # every plane product at its largest magnitude
+    for hh, xx, ll, kc, cq, S in ops:
+        for sh in range(5, 20):
+            T = 256 * xx + ll + kc + cq + (1 << (sh - 1))
+            assert INT_MIN <= T <= INT_MAX
+            want = rshr(S, sh)
+            if INT_MIN <= want <= INT_MAX:
+                assert div_pow2_model(hh, T, sh) == want, (hh, T, sh)
+
+
+def test_attention_score_mixed_exponents():
+    """keys of a chunk with different exponents: the smallest shift sh0 = shq - max ek for the division, each key's own
+    rounding term 2^(shq - ek - 1) in T, then >> (b0 + max ek - ek)  ==  rshr(S, shq - ek)"""
+    rnd = random.Random(22)
+    for hh, xx, ll, kc, cq, S in _score_operands(rnd, 200):
+        for shq in range(7, 20):
+            for emax in range(0, min(4, shq - 5) + 1):
+                a0 = min(shq - emax, 16)
+                b0 = shq - emax - a0
+                for ek in range(0, emax + 1):
+                    T = 256 * xx + ll + kc + cq + ((1 << (shq - 1)) >> ek)
+                    got = s32(hh * (1 << (16 - a0)) + mulhi32(T, 1 << (32 - a0))) >> (b0 + emax - ek)
+                    assert got == rshr(S, shq - ek), (shq, emax, ek)
+
+
+def exp_lut_ref(z, L):
+    """src/kernels.cu:671-722 lut_exp: 0 from z = 2^20 on, else L[i] + ((L[i+1] - L[i]) f >> 10), truncated to int32"""
+    if z >= 1 << 20:
+        return 0
+    i, f = z >> 10, z & 1023
+    return s32(L[i] + (((L[i + 1] - L[i]) * f) >> 10))
+
+
+def exp_fast_model(z, L):
+    """attn.cu exp_fast: zc = min(z, 2^20); entry (L[i], 2 (L[i+1] - L[i])), sentinel (0, 0) at 1024;
+    E = mad.hi.s32(2 D, f 2^21, L[i])"""
+    zc = min(z, 1 << 20)
+    i, f = zc >> 10, zc & 1023
+    Li, D2 = (L[i], 2 * (L[i + 1] - L[i])) if i < 1024 else (0, 0)
+    assert INT_MIN <= D2 <= INT_MAX and 0 <= f << 21 < 2**31
+    return s32(mulhi32(D2, f << 21) + Li)
+
+
+def test_attention_exp_table_fast_form():
+    import math
+    rnd = random.Random(23)
+    tables = [[round(2**30 * math.exp(-i / 64.0)) for i in range(1025)]]
+    # random tables that still qualify: values in [0, 2^31), neighbour differences below 2^30
+    for _ in range(3):
+        t = [rnd.randint(0, 2**31 - 1)]
+        for _ in range(1024):
+            t.append(min(2**31 - 1, max(0, t[-1] + rnd.randint(-(2**30) + 1, 2**30 - 1))))
+        tables.append(t)
+    for L in tables:
+        assert all(0 <= v < 2**31 for v in L) and all(abs(L[i + 1] - L[i]) < 2**30 for i in range(1024))
+        zs = [0, 1, 1023, 1024, (1 << 20) - 1, 1 << 20, (1 << 20) + 5, 2**32 - 1] + [rnd.randint(0, 1 << 20) for _ in range(3000)]
+        for z in zs:
+            assert exp_fast_model(z, L) == exp_lut_ref(z, L), z
+
+
+def test_attention_p_short_form():
+    """P = min(32767, (E r + 2^46) >> 47) with r = floor(2^62 / sum E) == min(32767, (E rhi + hi32(E rlo) + 2^14) >> 15)"""
+    rnd = random.Random(24)
+    for _ in range(3000):
+        n = rnd.randint(1, 4096)
+        Es = [rnd.choice([0, 2**30, rnd.randint(0, 2**30), rnd.randint(0, 1000)]) for _ in range(min(n, 8))]
+        tot = sum(Es) + rnd.randint(0, (n - len(Es)) * 2**30 if n > len(Es) else 0)
+        if tot == 0:
+            continue
+        r = (1 << 62) // tot
+        rhi, rlo = r >> 32, r & 0xFFFFFFFF
+        for E in Es:
+            want = min(32767, (E * r + (1 << 46)) >> 47)
+            h = (E * rhi + ((E * rlo) >> 32) + 16384) & 0xFFFFFFFF
+            assert min(h >> 15, 32767) == want

@@ -17,8 +17,13 @@
 //       P = 256 ph + pl + 128 with ph = P >> 8, pl = (P & 255) - 128 written to shared memory by the
 //       softmax warps as the A operand; A = Ph.Vh, Y = Ph.Vl + Pl.Vh, D = Pl.Vl (K-major V^T tiles);
 //       n = number of keys swept (padded keys carry V = 0 and P = 0).
+// Softmax arithmetic per score element (the CUDA-core work that bounds the kernel): the score in 32-bit wrapping
+// arithmetic as (hh M + (T >> a)) >> b (see div_pow2), the exp table interpolated with one mad.hi on entries
+// (L[i], 2 (L[i+1] - L[i])), and P from two multiply-adds of E with the 64-bit reciprocal's halves; the integer work is
+// split between the ALU and FMA pipes.  A per-stage aux warp turns each K tile's ksum into int32 and the 16-key
+// quarters' exponent ranges once per CTA, so the softmax warps only read them.
 // Warp roles: warp 0 TMA (Q once; K tiles + per-key ek/ksum each pass; V^T tiles in pass 2),
-// warp 1 TMEM allocation + MMA issue, warps 2..17 softmax (thread = one query row = one TMEM
+// warp 1 TMEM allocation + MMA issue, warp 18 per-stage key data, warps 2..17 softmax (thread = one query row = one TMEM
 // lane; the four warps of a lane quarter split each 64-key tile, and the output dims, in quarters).
 // TMEM: QK buffers at columns [0,192) and [192,384) (passes 0-1 alternate; pass 2 uses the first),
 // P.V accumulators at [192,384) during pass 2.  All barrier waits are bounded.
@@ -46,17 +51,23 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KS * KSTAGE;
 constexpr int OFF_P = OFF_V + VS * VSTAGE;
-constexpr int OFF_KAUX = OFF_P + 2 * P_BYTES;          // per K stage: ek int32[64], ksum int64[64]
-constexpr int KAUX_BYTES = 64 * 4 + 64 * 8;
-constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025]: (L[i], L[i+1] - L[i]); entry 1024 = (0, 0)
+constexpr int OFF_KAUX = OFF_P + 2 * P_BYTES;          // per K stage: ek int32[64], ksum int64[64] (TMA), then the aux
+constexpr int KAUX_TMA = 64 * 4 + 64 * 8;              // warp's kc int32[64] (= 128 ksum) and per 16-key quarter (min ek, max ek)
+constexpr int KAUX_KC = KAUX_TMA, KAUX_QI = KAUX_KC + 64 * 4;
+constexpr int KAUX_BYTES = KAUX_QI + 4 * 8;
+constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025] exp table (see exp_fast / exp_general); entry 1024 = (0, 0)
 constexpr int SW = 16;                                 // softmax warps: four per TMEM lane quarter, 16 keys each
-constexpr int THREADS = 32 * (2 + SW);
+constexpr int AUX_WARP = 2 + SW;                      // per K stage: kc and the quarters' exponent range, once per CTA
+constexpr int THREADS = 32 * (3 + SW);
 constexpr int OFF_RED = OFF_LUT + 1032 * 8;            // cross-warp reductions: 4 x 128 x 8 bytes
-constexpr int OFF_WK = OFF_RED + 4 * 128 * 8;          // per softmax warp: ek[16], 128*ksum[16] of its keys
-constexpr int OFF_BAR = OFF_WK + SW * 32 * 4;
-constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+constexpr int OFF_BAR = OFF_RED + 4 * 128 * 8;
+constexpr int NBAR = 1 + 3 * KS + 2 * VS + 2 + 2 + 2 + 1;
 constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;
 constexpr int TMEM_COLS = 512;
+
+// Constants the softmax multiplies by, passed as kernel arguments so the compiler keeps the multiply forms on the FMA
+// pipe instead of turning them into shifts and adds on the ALU pipe: 1, 256, 2^21, 8.
+struct OpK { int c1, c256, c2p21, c8; };
 
 struct AttnArgs {
     CUtensorMap tmQh, tmQl, tmKh, tmKl, tmVh, tmVl;
@@ -69,6 +80,7 @@ struct AttnArgs {
     unsigned* err;
     long long wait_limit;          // SM clock cycles before a barrier wait gives up
     int stall;                     // failure-path tests: the TMA producer issues nothing
+    OpK k;                         // the constants 1, 256, 2^21 and 8 (see OpK)
 };
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -76,113 +88,245 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
-// s = sat32(rshr(65536 hh + T, sh)) for a shift sh in [5, 19], T = 256 xx + ll + cq + 128 ksum + 2^(sh-1) (the
-// rounding term already added).  |S| < 2^36 (64 products of 16-bit values), so S fits 64 bits, S / 2^5 fits 32 bits
-// and no saturation can occur: one wide multiply-add and one funnel shift of the 64-bit sum.
-__device__ __forceinline__ int score_fast(int hh, int T, int sh) {
-    const long long S = (long long)hh * 65536 + T;
-    return int(__funnelshift_r(uint32_t(S), uint32_t(S >> 32), sh));
+// ---- integer building blocks with a chosen pipe.  The softmax's integer work is split between the two integer pipes
+// of the SM sub-partition (each issues a warp instruction every other cycle): multiplies, multiply-highs (right shifts
+// by a power of two) and multiply-adds run on the FMA pipe, adds / min / max / logic / funnel shifts on the ALU pipe.
+// The multipliers that are powers of two come from kernel arguments (OpK), so the compiler keeps the multiply forms.
+__device__ __forceinline__ int mad_lo(int a, int b, int c) { int d; asm("mad.lo.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ int mul_lo(int a, int b) { int d; asm("mul.lo.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d; }
+__device__ __forceinline__ int mad_hi(int a, int b, int c) { int d; asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ int mul_hi(int a, int b) { int d; asm("mul.hi.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d; }
+__device__ __forceinline__ uint32_t mad_hi_u(uint32_t a, uint32_t b, uint32_t c) { uint32_t d; asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ uint32_t mad_lo_u(uint32_t a, uint32_t b, uint32_t c) { uint32_t d; asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
+__device__ __forceinline__ uint64_t mad_wide_u(uint32_t a, uint32_t b, uint64_t c) { uint64_t d; asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c)); return d; }
+__device__ __forceinline__ int2 lds_v2(uint32_t addr) { int2 v; asm("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr)); return v; }
+
+// ---- score arithmetic (fast forms; every shift sh = 19 - eq - ek of the chunk lies in [5, 19])
+// s = floor((65536 hh + T) / 2^sh) with T = 256 xx + ll + cq + 128 ksum + 2^(sh-1) (the rounding term included; |T| < 2^31)
+// is computed in 32 bits as  s = (hh M + (T >> a)) >> b  with a = min(sh, 16), b = sh - a, M = 2^(16 - a):
+//   sh <= 16: 65536 hh = 2^sh (hh M), so the quotient is hh M + floor(T / 2^sh);
+//   sh > 16:  floor(floor((65536 hh + T) / 2^16) / 2^b) = (hh + (T >> 16)) >> b.
+// |s| < 2^31 (|S| < 2^36, sh >= 5), so hh M + (T >> a) is formed modulo 2^32: an intermediate wrap cancels.  T >> a is
+// the multiply-high of T by 2^(32 - a) (a >= 5, so the multiplier is a positive int32).
+// A chunk whose keys have different exponents takes the smallest shift sh0 = 19 - eq - max ek for the division
+// and shifts each key's result right by the remainder d = max ek - ek (nested floors), with each key's own rounding
+// term 2^(19 - eq - ek - 1) in T.
+struct ShiftSplit { int a, b; int M, A; };
+__device__ __forceinline__ ShiftSplit split_shift(int sh) {
+    const int a = min(sh, 16);
+    return ShiftSplit{a, sh - a, 1 << (16 - a), 1 << (32 - a)};
+}
+__device__ __forceinline__ int div_pow2(int hh, int T, const ShiftSplit& p) { return mad_lo(hh, p.M, mul_hi(T, p.A)); }
+
+// ---- exp table: E = L[i] + floor((L[i+1] - L[i]) f / 2^10) for z = mx - s, i = min(z, 2^20) >> 10, f = its low 10 bits
+// (index 1024 is a sentinel (0, 0): E = 0 from z = 2^20 on).  Fast table (every L[i] in [0, 2^31) and every difference
+// below 2^30 in magnitude): entries (L[i], 2 (L[i+1] - L[i])) and E = hi32(2 D * f 2^21) + L[i] in one mad.hi.
+// General table: entries (L[i], L[i+1]) and the difference in 64 bits, exactly as the reference does.
+__device__ __forceinline__ uint32_t zclamp(int mx, int s) { return min(uint32_t(mx) - uint32_t(s), 1u << 20); }
+__device__ __forceinline__ int exp_fast(uint32_t zc, uint32_t lut_addr, const OpK& k) {
+    const int2 e = lds_v2(uint32_t(mad_lo(int(zc >> 10), k.c8, int(lut_addr))));
+    return mad_hi(e.y, mul_lo(int(zc & 1023u), k.c2p21), e.x);
+}
+__device__ __forceinline__ int exp_general(uint32_t zc, const int2* __restrict__ T) {
+    const int2 e = T[zc >> 10];
+    return int(i64(e.x) + (((i64(e.y) - e.x) * int(zc & 1023u)) >> 10));
+}
+// P = min(32767, (E r + 2^46) >> 47) for 0 <= E <= sum E, r = floor(2^62 / sum E) = rhi 2^32 + rlo: E r <= 2^62, so
+// floor((E r + 2^46) / 2^47) = floor((E rhi + hi32(E rlo) + 2^14) / 2^15), every term below 2^32.
+__device__ __forceinline__ int p_of(uint32_t E, uint32_t rlo, uint32_t rhi) {
+    const uint32_t h = mad_lo_u(E, rhi, mad_hi_u(E, rlo, 16384u));
+    return int(min(h >> 15, 32767u));
+}
+// the same for any table: E may be negative; the reference's int64 arithmetic with P = 0 unless E > 0
+__device__ __forceinline__ int p_general(int E, uint64_t r) {
+    if (E <= 0) return 0;
+    const i64 p = (i64(E) * i64(r) + (i64(1) << 46)) >> 47;
+    return int(p > 32767 ? 32767 : p);
 }
 
-// E = expLUT(z) for z = mx - s >= 0 (z < 2^32): index min(z >> 10, 1024), the sentinel entry 1024 = (0, 0) giving
-// E = 0 from z = 2^20 on; linear interpolation over the low 10 bits.
-__device__ __forceinline__ int lut_exp(uint32_t z, const int2* L2) {
-    const int2 e = L2[min(z >> 10, 1024u)];
-    return e.x + int(((long long)e.y * int(z & 1023u)) >> 10);
-}
+// Per-chunk row data of one thread: shq = 19 - eq, cq = 32768 qhs + 128 qls, r0 = 2^(shq - 1).
+struct RowK { int shq, cq, r0; };
 
-// One 16-key quarter tile of one pass for one query row (this thread) -- scores from the three TMEM accumulators
-// (HH at taddr, X at +64, LL at +128), then PASS 0: row max; PASS 1: sum of E; PASS 2: P (into pw_h / pw_l).
-template <int PASS>
-__device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ wk, int shq, int r0, int cq, bool fast, bool unif, int eku,
-                                             bool full, int kbase, int q, int Tk, int causal, const int2* __restrict__ L2,
+// One 16-key quarter tile of one pass for one query row (this thread): scores from the three TMEM accumulators
+// (HH at taddr, X at +64, LL at +128; ekp / kcp = the 16 keys' exponents and 128 ksum), then
+// PASS 0: row max; PASS 1: sum of E; PASS 2: P (into pw_h / pw_l).  TF: the fast exp table; FULL: every key of the
+// chunk is valid (no causal mask, no key past Tk), else invalid keys take E = 0 and do not enter the max.
+// mode 0: one key exponent eku for the chunk; 1: exponents differ (eku = their max); 2: a shift outside [5, 19].
+template <int PASS, bool TF, bool FULL>
+__device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ ekp, const int* __restrict__ kcp, const RowK& rk, int mode, int eku,
+                                             int kbase, int q, int Tk, int causal, const int2* __restrict__ L2, uint32_t lut_addr, const OpK& k,
                                              int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l,
-                                             uint64_t* rel_qk, uint64_t* rel_k) {
-    // X and LL first, folded into T (16 registers), then HH: the three accumulators are never all live at once
+                                             uint64_t* rel_qk) {
     int s[16];
+    bool pre_shift = false;          // PASS 0, mode 0: s holds hh M + (T >> a); the row max takes the >> b once per chunk
+    int bsh = 0;
+    const ShiftSplit p = split_shift(mode == 2 ? 16 : rk.shq - eku);
+    // X and LL first, folded into T (16 registers), then HH: the three accumulators are never all live at once
     {
         int xx[16], ll[16];
         tmem_ld16(taddr + 64, xx); tmem_ld16(taddr + 128, ll);
         tmem_ld_wait();
-        if (fast && unif) {
-            const int cr = cq + (r0 >> eku);       // one key exponent for the chunk: rounding term of shift shq - eku
+        if (mode == 0) {
+            const int cr = rk.cq + (1 << (rk.shq - eku - 1));
             #pragma unroll
             for (int u = 0; u < 16; u += 4) {
-                const int4 k4 = *reinterpret_cast<const int4*>(wk + 16 + u);
-                s[u] = (xx[u] << 8) + (ll[u] + k4.x + cr); s[u + 1] = (xx[u + 1] << 8) + (ll[u + 1] + k4.y + cr);
-                s[u + 2] = (xx[u + 2] << 8) + (ll[u + 2] + k4.z + cr); s[u + 3] = (xx[u + 3] << 8) + (ll[u + 3] + k4.w + cr);
+                const int4 k4 = *reinterpret_cast<const int4*>(kcp + u);
+                s[u] = mad_lo(xx[u], k.c256, ll[u] + k4.x + cr); s[u + 1] = mad_lo(xx[u + 1], k.c256, ll[u + 1] + k4.y + cr);
+                s[u + 2] = mad_lo(xx[u + 2], k.c256, ll[u + 2] + k4.z + cr); s[u + 3] = mad_lo(xx[u + 3], k.c256, ll[u + 3] + k4.w + cr);
             }
-        } else if (fast) {
+        } else if (mode == 1) {          // each key's own rounding term 2^(shq - ek - 1) = r0 >> ek
             #pragma unroll
             for (int u = 0; u < 16; u += 4) {
-                const int4 e4 = *reinterpret_cast<const int4*>(wk + u);
-                const int4 k4 = *reinterpret_cast<const int4*>(wk + 16 + u);
-                s[u] = (xx[u] << 8) + (ll[u] + k4.x + cq) + (r0 >> e4.x); s[u + 1] = (xx[u + 1] << 8) + (ll[u + 1] + k4.y + cq) + (r0 >> e4.y);
-                s[u + 2] = (xx[u + 2] << 8) + (ll[u + 2] + k4.z + cq) + (r0 >> e4.z); s[u + 3] = (xx[u + 3] << 8) + (ll[u + 3] + k4.w + cq) + (r0 >> e4.w);
+                const int4 e4 = *reinterpret_cast<const int4*>(ekp + u);
+                const int4 k4 = *reinterpret_cast<const int4*>(kcp + u);
+                s[u] = mad_lo(xx[u], k.c256, ll[u] + k4.x + (rk.cq + (rk.r0 >> e4.x)));
+                s[u + 1] = mad_lo(xx[u + 1], k.c256, ll[u + 1] + k4.y + (rk.cq + (rk.r0 >> e4.y)));
+                s[u + 2] = mad_lo(xx[u + 2], k.c256, ll[u + 2] + k4.z + (rk.cq + (rk.r0 >> e4.z)));
+                s[u + 3] = mad_lo(xx[u + 3], k.c256, ll[u + 3] + k4.w + (rk.cq + (rk.r0 >> e4.w)));
             }
         } else {
             #pragma unroll
-            for (int u = 0; u < 16; ++u) s[u] = (xx[u] << 8) + ll[u] + cq + wk[16 + u];
+            for (int u = 0; u < 16; ++u) s[u] = xx[u] * 256 + ll[u] + rk.cq + kcp[u];
         }
     }
     {
         int hh[16];
         tmem_ld16(taddr, hh);
         tmem_ld_wait();
-        if (fast && unif) {
-            const int sh = shq - eku;
+        // every accumulator of the tile is in registers: hand the QK buffer back now, so the next tile's QK products
+        // run on the tensor core while this tile's arithmetic runs here (the K stage, whose per-key data is still
+        // read below, is handed back by the caller)
+        tc_fence_before();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(rel_qk);
+        if (mode == 0) {
             #pragma unroll
-            for (int u = 0; u < 16; ++u) s[u] = score_fast(hh[u], s[u], sh);
-        } else if (fast) {
+            for (int u = 0; u < 16; ++u) s[u] = div_pow2(hh[u], s[u], p);
+            if (PASS == 0 && FULL) { pre_shift = true; bsh = p.b; }
+            else if (__any_sync(0xffffffffu, p.b != 0)) {
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) s[u] >>= p.b;
+            }
+        } else if (mode == 1) {
+            const int bb = p.b + eku;                         // key u: >> (b + max ek - ek_u)
             #pragma unroll
-            for (int u = 0; u < 16; ++u) s[u] = score_fast(hh[u], s[u], shq - wk[u]);
-        } else {            // a shift outside [5, 19] somewhere in the tile: the 64-bit rshr with saturation
+            for (int u = 0; u < 16; u += 4) {
+                const int4 e4 = *reinterpret_cast<const int4*>(ekp + u);
+                s[u] = div_pow2(hh[u], s[u], p) >> (bb - e4.x); s[u + 1] = div_pow2(hh[u + 1], s[u + 1], p) >> (bb - e4.y);
+                s[u + 2] = div_pow2(hh[u + 2], s[u + 2], p) >> (bb - e4.z); s[u + 3] = div_pow2(hh[u + 3], s[u + 3], p) >> (bb - e4.w);
+            }
+        } else {          // a shift outside [5, 19] somewhere in the tile: the 64-bit rshr with saturation
             #pragma unroll
-            for (int u = 0; u < 16; ++u) s[u] = int(rshr((i64(hh[u]) << 16) + s[u], shq - wk[u]));
+            for (int u = 0; u < 16; ++u) s[u] = int(rshr((i64(hh[u]) << 16) + s[u], rk.shq - ekp[u]));
         }
     }
-    // every accumulator of the tile is in registers: hand the QK buffer and the K stage back now, so the next
-    // tile's QK products run on the tensor core while this tile's E / P arithmetic runs here
-    tc_fence_before();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) { mbar_arrive(rel_qk); mbar_arrive(rel_k); }
     uint32_t vmask = 0xFFFFu;   // validity by key position (a valid score may itself saturate to INT_MIN)
-    if (!full) {
+    if (!FULL) {
         vmask = 0;
         #pragma unroll
         for (int u = 0; u < 16; ++u) { const int key = kbase + u; vmask |= uint32_t(key < Tk && !(causal && key > q)) << u; }
     }
     if constexpr (PASS == 0) {
-        if (!full) {
+        if (pre_shift) {
+            int m = s[0];
             #pragma unroll
-            for (int u = 0; u < 16; ++u) s[u] = (vmask >> u) & 1u ? s[u] : INT_MIN;
+            for (int u = 1; u < 16; ++u) m = max(m, s[u]);
+            mx = max(mx, m >> bsh);
+        } else {
+            if (!FULL) {
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) s[u] = (vmask >> u) & 1u ? s[u] : INT_MIN;
+            }
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
         }
-        #pragma unroll
-        for (int u = 0; u < 16; ++u) mx = max(mx, s[u]);
     } else if constexpr (PASS == 1) {
-        // each E < 2^31 (the table holds int32 values >= 0): a pair fits 32 bits
-        #pragma unroll
-        for (int u = 0; u < 16; u += 2) {
-            uint32_t e0 = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u]), L2)), e1 = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u + 1]), L2));
-            if (!full) { e0 = (vmask >> u) & 1u ? e0 : 0u; e1 = (vmask >> (u + 1)) & 1u ? e1 : 0u; }
-            sum += e0 + e1;
+        if constexpr (TF) {
+            // each E < 2^31: a pair fits 32 bits, added to the 64-bit sum by one wide multiply-add
+            #pragma unroll
+            for (int u = 0; u < 16; u += 2) {
+                int e0 = exp_fast(zclamp(mx, s[u]), lut_addr, k), e1 = exp_fast(zclamp(mx, s[u + 1]), lut_addr, k);
+                if (!FULL) { e0 = (vmask >> u) & 1u ? e0 : 0; e1 = (vmask >> (u + 1)) & 1u ? e1 : 0; }
+                sum = mad_wide_u(uint32_t(mad_lo(e0, k.c1, e1)), uint32_t(k.c1), sum);
+            }
+        } else {
+            #pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int e = exp_general(zclamp(mx, s[u]), L2);
+                if ((vmask >> u) & 1u) sum += uint64_t(i64(e));
+            }
         }
     } else {
-        // P = min(32767, (E r + 2^46) >> 47) with r = rhi 2^32 + rlo.  E <= sum E, so E r <= 2^62 and
-        // floor(E r / 2^32) = E rhi + umulhi(E, rlo) <= 2^30 fits 32 bits.  Four keys at a time, packed at once.
         #pragma unroll
         for (int u = 0; u < 16; u += 4) {
             int P[4];
             #pragma unroll
             for (int w = 0; w < 4; ++w) {
-                uint32_t e = uint32_t(lut_exp(uint32_t(mx) - uint32_t(s[u + w]), L2));
-                if (!full) e = (vmask >> (u + w)) & 1u ? e : 0u;
-                const uint32_t h = e * rhi + (__umulhi(e, rlo) + 16384u);
-                P[w] = int(min(32767u, h >> 15));
-                psum += P[w];
+                if constexpr (TF) P[w] = p_of(uint32_t(exp_fast(zclamp(mx, s[u + w]), lut_addr, k)), rlo, rhi);
+                else P[w] = p_general(exp_general(zclamp(mx, s[u + w]), L2), (uint64_t(rhi) << 32) | rlo);
+                if (!FULL) P[w] = (vmask >> (u + w)) & 1u ? P[w] : 0;
+                psum = mad_lo(P[w], k.c1, psum);
             }
-            pw_h[u / 4] = pack_hi4(P[0], P[1], P[2], P[3]);
-            pw_l[u / 4] = pack_lo4(P[0], P[1], P[2], P[3]);
+            // 0 <= P < 2^15: the four 16-bit values as two words, then their hi bytes and (lo bytes - 128)
+            const uint32_t w01 = __byte_perm(uint32_t(P[0]), uint32_t(P[1]), 0x5410), w23 = __byte_perm(uint32_t(P[2]), uint32_t(P[3]), 0x5410);
+            pw_h[u / 4] = __byte_perm(w01, w23, 0x7531);
+            pw_l[u / 4] = __byte_perm(w01, w23, 0x6420) ^ 0x80808080u;
+        }
+    }
+}
+
+// Per-thread constants of the softmax warps and their running row state.
+struct SoftCtx {
+    uint64_t *qk_full, *qk_free, *k_empty, *kinfo_full, *p_full, *p_free;
+    const uint8_t* kaux;            // stage 0 of the per-stage key data
+    const int2* lut;
+    uint32_t lut_addr;              // shared-memory address of the exp table
+    uint8_t *pst_h, *pst_l;         // this thread's 16 P bytes in the hi / lo P tiles (pass 2)
+    uint32_t tq;                    // TMEM address of this thread's lane quarter and key quarter in QK buffer 0
+    RowK rk;
+    int shq_min, kq, q, nT;
+};
+struct SoftState { int mx; uint64_t sum; uint32_t rlo, rhi; int psum; bool ok; };
+
+// One pass over every key tile for this thread's row and key quarter.  Every warp runs every iteration, also after
+// a timed-out wait (it then skips the work), so the barriers' arrival counts stay consistent.
+template <int PASS, bool TF>
+__device__ __forceinline__ void softmax_pass(const AttnArgs& a, const SoftCtx& c, SoftState& st) {
+    const int lane = threadIdx.x & 31;
+    for (int j = 0; j < c.nT; ++j) {
+        const int it = PASS * c.nT + j, ks = it % KS;
+        const int b = PASS < 2 ? (it & 1) : 0;
+        const int ub = PASS < 2 ? (it >> 1) : it - c.nT;           // earlier uses of buffer b
+        if (st.ok) st.ok = __all_sync(0xffffffffu, mbar_wait(&c.qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
+        if (st.ok) st.ok = __all_sync(0xffffffffu, mbar_wait(&c.kinfo_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
+        if (!st.ok) continue;
+        tc_fence_after();
+        const uint8_t* aux = c.kaux + ks * KAUX_BYTES;
+        const int2 qi = reinterpret_cast<const int2*>(aux + KAUX_QI)[c.kq];      // (min, max) key exponent of the quarter
+        const int kbase = j * 64 + c.kq * 16;
+        const bool full = !a.causal && kbase + 16 <= a.Tk;
+        const int mode = c.shq_min - qi.y < 5 ? 2 : (qi.x == qi.y ? 0 : 1);   // fast forms need every shift in [5, 19]
+        uint32_t pw_h[4], pw_l[4];
+        const int* ekp = reinterpret_cast<const int*>(aux) + c.kq * 16;
+        const int* kcp = reinterpret_cast<const int*>(aux + KAUX_KC) + c.kq * 16;
+        if (full) softmax_tile<PASS, TF, true>(c.tq + uint32_t(b * 192), ekp, kcp, c.rk, mode, qi.y, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
+                                               st.mx, st.sum, st.rlo, st.rhi, st.psum, pw_h, pw_l, &c.qk_free[b]);
+        else softmax_tile<PASS, TF, false>(c.tq + uint32_t(b * 192), ekp, kcp, c.rk, mode, qi.y, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
+                                           st.mx, st.sum, st.rlo, st.rhi, st.psum, pw_h, pw_l, &c.qk_free[b]);
+        bool pout = false;
+        if (PASS == 2) {
+            st.ok = __all_sync(0xffffffffu, mbar_wait(c.p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit));
+            if (st.ok) {
+                *reinterpret_cast<uint4*>(c.pst_h) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
+                *reinterpret_cast<uint4*>(c.pst_l) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
+                fence_async_smem();
+                pout = true;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (pout) mbar_arrive(c.p_full);
+            mbar_arrive(&c.k_empty[ks]);      // this warp has read the stage's per-key data
         }
     }
 }
@@ -197,6 +341,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     uint64_t* qk_full = v_empty + VS; uint64_t* qk_free = qk_full + 2;
     uint64_t* p_full = qk_free + 2; uint64_t* p_free = p_full + 1;
     uint64_t* pv_done = p_free + 1;
+    uint64_t* kinfo_full = pv_done + 1;                   // [KS] the aux warp has written stage ks's kc / exponent ranges
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
     int2* lut2 = reinterpret_cast<int2*>(sm + OFF_LUT);
 
@@ -210,13 +355,25 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         for (int s = 0; s < VS; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&qk_full[b], 1); mbar_init(&qk_free[b], SW); }
         mbar_init(p_full, SW); mbar_init(p_free, 1); mbar_init(pv_done, 1);
+        for (int s = 0; s < KS; ++s) mbar_init(&kinfo_full[s], 1);
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+    // exp table: (L[i], L[i+1]) staged, and whether it qualifies for the fast form (every L[i] >= 0 and every
+    // difference below 2^30 in magnitude); then the fast form replaces L[i+1] by 2 (L[i+1] - L[i])
+    int tf = 1;
     for (int i = threadIdx.x; i <= 1024; i += blockDim.x) {
-        if (i < 1024) { const int x0 = __ldg(a.lexp + i), x1 = __ldg(a.lexp + i + 1); lut2[i] = make_int2(x0, x1 - x0); }
-        else lut2[i] = make_int2(0, 0);
+        int2 v = make_int2(0, 0);
+        if (i < 1024) {
+            v = make_int2(__ldg(a.lexp + i), __ldg(a.lexp + i + 1));
+            const i64 d = i64(v.y) - v.x;
+            tf &= v.x >= 0 && v.y >= 0 && d < (i64(1) << 30) && d > -(i64(1) << 30);
+        }
+        lut2[i] = v;
     }
+    const bool tfast = __syncthreads_and(tf) != 0;
+    if (tfast)
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) lut2[i].y = 2 * (lut2[i].y - lut2[i].x);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -233,7 +390,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 if (!mbar_wait(&k_empty[ks], ((it / KS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) break;
                 uint8_t* kst = sm + OFF_K + ks * KSTAGE;
                 uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
-                mbar_arrive_expect_tx(&k_full[ks], KSTAGE + KAUX_BYTES);
+                mbar_arrive_expect_tx(&k_full[ks], KSTAGE + KAUX_TMA);
                 tma_load_2d(kst, &a.tmKh, &k_full[ks], 0, g * a.Tkp + j * 64);
                 tma_load_2d(kst + KT_BYTES, &a.tmKl, &k_full[ks], 0, g * a.Tkp + j * 64);
                 bulk_load(aux, a.ek + size_t(g) * a.Tkp + j * 64, 64 * 4, &k_full[ks]);
@@ -301,6 +458,31 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
             if (ok) ok = issue_pv(nT - 1);
             mma_commit(pv_done);
         }
+    } else if (warp == AUX_WARP) {
+        // ---------------------------------------------------------------- per-stage key data, once per CTA
+        // kc = 128 ksum as int32 (|ksum| <= 64 * 32767) and the (min, max) exponent of each 16-key quarter
+        bool ok = true;
+        for (int it = 0; it < nIt && ok; ++it) {
+            const int ks = it % KS;
+            ok = __all_sync(0xffffffffu, mbar_wait(&k_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
+            if (!ok) break;
+            uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
+            const int32_t* ek = reinterpret_cast<const int32_t*>(aux);
+            const i64* ksum = reinterpret_cast<const i64*>(aux + 256);
+            int32_t* kc = reinterpret_cast<int32_t*>(aux + KAUX_KC);
+            int2* qi = reinterpret_cast<int2*>(aux + KAUX_QI);
+            const int e0 = ek[lane], e1 = ek[lane + 32];            // quarters lane >> 4 and 2 + (lane >> 4)
+            kc[lane] = int(128 * ksum[lane]); kc[lane + 32] = int(128 * ksum[lane + 32]);
+            int mn0 = e0, mx0 = e0, mn1 = e1, mx1 = e1;
+            #pragma unroll
+            for (int o = 8; o; o >>= 1) {
+                mn0 = min(mn0, __shfl_xor_sync(0xffffffffu, mn0, o)); mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mn1 = min(mn1, __shfl_xor_sync(0xffffffffu, mn1, o)); mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
+            if ((lane & 15) == 0) { qi[lane >> 4] = make_int2(mn0, mx0); qi[2 + (lane >> 4)] = make_int2(mn1, mx1); }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&kinfo_full[ks]);
+        }
     } else {
         // ---------------------------------------------------------------- softmax / output warps
         const int qq = warp & 3, kq = (warp - 2) >> 2;             // lane quarter; key quarter (and dim quarter)
@@ -310,67 +492,38 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         const int eqv = __ldg(a.eq + rq);
         const int cq = int(32768 * __ldg(a.qhs + rq) + 128 * __ldg(a.qls + rq));
         const int shq = 19 - eqv;                                   // eq <= 17, so shq >= 2
-        const int r0 = 1 << (shq - 1);                              // rounding term of shift shq; >> ek gives that of shq - ek
-        const int shq_min = __reduce_min_sync(0xffffffffu, shq);
-        int* wk = reinterpret_cast<int*>(sm + OFF_WK) + (warp - 2) * 32;
+        SoftCtx c;
+        c.qk_full = qk_full; c.qk_free = qk_free; c.k_empty = k_empty; c.kinfo_full = kinfo_full; c.p_full = p_full; c.p_free = p_free;
+        c.kaux = sm + OFF_KAUX; c.lut = lut2; c.lut_addr = smem_u32(lut2);
+        c.pst_h = sm + OFF_P + sw64_off(rl, kq); c.pst_l = c.pst_h + P_BYTES;
+        c.tq = tmem + tl + uint32_t(kq * 16);
+        c.rk = RowK{shq, cq, 1 << (shq - 1)};                       // r0: rounding term of shift shq; >> ek gives that of shq - ek
+        c.shq_min = __reduce_min_sync(0xffffffffu, shq);
+        c.kq = kq; c.q = q; c.nT = nT;
         i64* red = reinterpret_cast<i64*>(sm + OFF_RED);          // [4][128]
-        int mx = INT_MIN; uint64_t sum = 0; uint32_t rlo = 0, rhi = 0; int psum = 0;
-        bool ok = true;
-        // Every warp runs all iterations and every named barrier, also after a timed-out wait
-        // (then it skips the work), so no warp can be left waiting on a barrier the others skipped.
-        for (int pass = 0; pass < 3; ++pass) {
-            for (int j = 0; j < nT; ++j) {
-                const int it = pass * nT + j, ks = it % KS;
-                const int b = pass < 2 ? (it & 1) : 0;
-                const int ub = it < 2 * nT ? (it >> 1) : it - nT;      // earlier uses of buffer b
-                if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
-                if (ok) {
-                    tc_fence_after();
-                    // this warp's 16 keys: exponent and 128 * ksum, staged once per tile for vector reads
-                    const uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
-                    const int kk = kq * 16 + (lane & 15);
-                    const int ekL = reinterpret_cast<const int32_t*>(aux)[kk];
-                    const int kcL = int(128 * reinterpret_cast<const i64*>(aux + 256)[kk]);
-                    const int emax = __reduce_max_sync(0xffffffffu, ekL), emin = __reduce_min_sync(0xffffffffu, ekL);
-                    if (lane < 16) { wk[lane] = ekL; wk[16 + lane] = kcL; }
-                    __syncwarp();
-                    const int kbase = j * 64 + kq * 16;
-                    const bool full = !a.causal && kbase + 16 <= a.Tk;
-                    const bool fast = shq_min - emax >= 5;           // every shift of the tile in [5, 19]
-                    const uint32_t taddr = tmem + tl + uint32_t(b * 192 + kq * 16);
-                    uint32_t pw_h[4], pw_l[4];                        // P bytes of this thread's 16 keys (pass 2)
-                    const bool unif = emin == emax;
-                    if (pass == 0) softmax_tile<0>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
-                    else if (pass == 1) softmax_tile<1>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
-                    else softmax_tile<2>(taddr, wk, shq, r0, cq, fast, unif, emax, full, kbase, q, a.Tk, a.causal, lut2, mx, sum, rlo, rhi, psum, pw_h, pw_l, &qk_free[b], &k_empty[ks]);
-                    if (pass == 2) {
-                        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit));
-                        if (ok) {
-                            uint8_t* php = sm + OFF_P; uint8_t* plp = php + P_BYTES;
-                            *reinterpret_cast<uint4*>(php + sw64_off(rl, kq)) = make_uint4(pw_h[0], pw_h[1], pw_h[2], pw_h[3]);
-                            *reinterpret_cast<uint4*>(plp + sw64_off(rl, kq)) = make_uint4(pw_l[0], pw_l[1], pw_l[2], pw_l[3]);
-                            fence_async_smem();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(p_full);
-                        }
-                    }
-                }
-                if (j == nT - 1 && pass < 2) {         // combine the four key quarters of each row
-                    red[kq * 128 + rl] = pass == 0 ? i64(mx) : i64(sum);
-                    asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
-                    i64 o[3];
-                    #pragma unroll
-                    for (int w = 1; w < 4; ++w) o[w - 1] = red[((kq + w) & 3) * 128 + rl];
-                    asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
-                    if (pass == 0) mx = max(max(mx, int(o[0])), max(int(o[1]), int(o[2])));
-                    else {
-                        const uint64_t tot = sum + uint64_t(o[0]) + uint64_t(o[1]) + uint64_t(o[2]);
-                        const uint64_t r = tot ? (uint64_t(1) << 62) / tot : 0;
-                        rlo = uint32_t(r); rhi = uint32_t(r >> 32);
-                    }
-                }
-            }
+        SoftState st{INT_MIN, 0, 0, 0, 0, true};
+        // combine the four key quarters of each row after pass 0 (max) and pass 1 (sum -> r)
+        auto combine = [&](i64 v, i64* o) {
+            red[kq * 128 + rl] = v;
+            asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
+            #pragma unroll
+            for (int w = 1; w < 4; ++w) o[w - 1] = red[((kq + w) & 3) * 128 + rl];
+            asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
+        };
+        i64 o[3];
+        if (tfast) softmax_pass<0, true>(a, c, st); else softmax_pass<0, false>(a, c, st);
+        combine(i64(st.mx), o);
+        st.mx = max(max(st.mx, int(o[0])), max(int(o[1]), int(o[2])));
+        if (tfast) softmax_pass<1, true>(a, c, st); else softmax_pass<1, false>(a, c, st);
+        combine(i64(st.sum), o);
+        {
+            const uint64_t tot = st.sum + uint64_t(o[0]) + uint64_t(o[1]) + uint64_t(o[2]);
+            const uint64_t r = tot ? (uint64_t(1) << 62) / tot : 0;
+            st.rlo = uint32_t(r); st.rhi = uint32_t(r >> 32);
         }
+        if (tfast) softmax_pass<2, true>(a, c, st); else softmax_pass<2, false>(a, c, st);
+        const bool ok = st.ok;
+        const int psum = st.psum;
         // ---------------------------------------------------------------- output
         red[kq * 128 + rl] = psum;
         asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
@@ -433,6 +586,7 @@ void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, cons
     a.err = o.err ? o.err : device_error_word(&g_attn_err);
     a.wait_limit = o.wait_limit > 0 ? o.wait_limit : WAIT_LIMIT_CYCLES;
     a.stall = o.stall;
+    a.k = OpK{1, 256, 1 << 21, 8};
     static std::atomic<int> attr_done[64];
     once_per_device(attr_done, [] { VELA_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)); });
     attn_kernel<<<dim3(ceil_div(Tqp, 128), G), THREADS, SMEM, st>>>(a);
