@@ -2,9 +2,11 @@
 // arena, the step's composition (noise -> UNet -> finalize), the text encoder / cross-attention K/V
 // of a prompt, CUDA-graph capture of the whole step and the two-slot submit / collect pipeline.
 //
-// Replaces the reference's DevModel / Engine (src/engine.h:16-124, src/engine.cu); the composition
-// follows src/engine.cu:389-490 (resnet, transformer, unet), :491-574 (text encoder, setPrompt) and
-// :599-677 (forwardIO, graph per slot, submit / collect / run).  Differences by design:
+// Replaces the reference's DevModel / Engine (src/engine.h:16-124, src/engine.cu).  The UNet is a table of blocks
+// (unet_plan) walked by one loop; it computes what src/engine.cu:389-490 computes, block for block, and also tells
+// the loader which weights are 3x3 kernels and which blocks are transformers.  The text encoder / setPrompt follow
+// src/engine.cu:491-574, the step and its pipeline :599-677 (forwardIO, graph per slot, submit / collect / run).
+// Differences by design:
 //   - every GEMM, convolution (implicit 3x3, any depth) and attention runs on the tcgen05 kernels;
 //     no cuBLASLt, no im2col buffer (except the 4-channel input conv), no score buffers;
 //   - weights are prepared once at load: 3x3 kernels permuted to tap-major K, N padded to 64,
@@ -14,9 +16,11 @@
 #include "ops.h"
 #include "host_util.h"
 #include "status.h"
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <set>
 #include <memory>
 #include <string>
 #include <vector>
@@ -72,12 +76,106 @@ private:
     std::map<std::string, PoisdEntry> entries_;
 };
 
+// ------------------------------------------------------------------ UNet topology as data
+// The step's blocks in execution order, built once from the SD-2.1 channel / head configuration.  Engine::unet walks
+// this table; the model loader uses it to find the 3x3 kernels and the transformer blocks.  Block order and tensor
+// names follow the reference's UNet (src/engine.cu:455-490), since every block output is compared with it.
+enum class BlockKind : uint8_t { ConvIn, Res, Xfmr, Down, Up, Out };
+struct UNetBlock {
+    BlockKind kind;
+    std::string name;        // tensor prefix in the model file
+    std::string tap;         // label of the block's output for the parity taps
+    int heads = 0;           // Xfmr: 64-dim attention heads
+    int xattn = -1;          // Xfmr: index of its prompt cross-attention K/V
+    bool push = false;       // the result is kept for the up path
+    bool pop = false;        // Res: the newest kept tensor is concatenated to the input first
+};
+static const std::vector<UNetBlock>& unet_plan() {
+    static const std::vector<UNetBlock> plan = [] {
+        std::vector<UNetBlock> p;
+        const int heads[4] = {5, 10, 20, 20};              // per level; width = 64 x heads (320, 640, 1280, 1280)
+        int xa = 0;
+        auto add = [&](BlockKind k, std::string name, std::string tap = std::string()) {
+            UNetBlock b; b.kind = k; b.tap = tap.empty() ? name : tap; b.name = std::move(name); p.push_back(std::move(b)); return &p.back();
+        };
+        auto attn = [&](std::string name, int h) { UNetBlock* b = add(BlockKind::Xfmr, std::move(name)); b->heads = h; b->xattn = xa++; return b; };
+        add(BlockKind::ConvIn, "unet.conv_in", "conv_in")->push = true;
+        for (int lv = 0; lv < 4; ++lv) {                       // down path: two resnets (+ attention above level 3)
+            const std::string db = "unet.down_blocks." + std::to_string(lv);
+            for (int r = 0; r < 2; ++r) {
+                UNetBlock* last = add(BlockKind::Res, db + ".resnets." + std::to_string(r));
+                if (lv < 3) last = attn(db + ".attentions." + std::to_string(r), heads[lv]);
+                last->push = true;
+            }
+            if (lv < 3) add(BlockKind::Down, db + ".downsamplers.0.conv")->push = true;
+        }
+        add(BlockKind::Res, "unet.mid_block.resnets.0");
+        attn("unet.mid_block.attentions.0", 20);
+        add(BlockKind::Res, "unet.mid_block.resnets.1");
+        for (int u = 0; u < 4; ++u) {                           // up path: three resnets on concatenated skips
+            const std::string ub = "unet.up_blocks." + std::to_string(u);
+            for (int r = 0; r < 3; ++r) {
+                add(BlockKind::Res, ub + ".resnets." + std::to_string(r))->pop = true;
+                if (u > 0) attn(ub + ".attentions." + std::to_string(r), heads[3 - u]);
+            }
+            if (u < 3) add(BlockKind::Up, ub + ".upsamplers.0.conv");
+        }
+        add(BlockKind::Out, "unet.conv_out", "eps");
+        return p;
+    }();
+    return plan;
+}
+static bool ends_with(const std::string& s, const char* suf) { const size_t l = std::strlen(suf); return s.size() >= l && s.compare(s.size() - l, l, suf) == 0; }
+// prefix of a transformer block's single inner block ("<name>.transformer_blocks.0")
+static std::string inner_block(const UNetBlock& b) { return b.name + ".transformer_blocks.0"; }
+
 // ------------------------------------------------------------------ device model
 struct Lin { int N = 0, K = 0, Np = 0, Kp = 0; bool conv3 = false; int8_t* w = nullptr; int32_t* cst = nullptr; };
 struct Norm { int C = 0; int32_t *g = nullptr, *beta = nullptr; i64 *g64 = nullptr, *beta64 = nullptr; i64 den = 0; };
 struct HostLin { int N = 0, K = 0, Np = 0, Kp = 0; bool conv3 = false; std::vector<int8_t> w; std::vector<int32_t> cst; };
 
-static bool ends(const std::string& s, const char* suf) { const size_t l = std::strlen(suf); return s.size() >= l && s.compare(s.size() - l, l, suf) == 0; }
+// The weights of the UNet's 3x3 kernels: every conv block of the plan and both convolutions of each resnet.
+static std::set<std::string> kernel3x3_names() {
+    std::set<std::string> out;
+    for (const UNetBlock& b : unet_plan()) {
+        if (b.kind == BlockKind::Res) { out.insert(b.name + ".conv1"); out.insert(b.name + ".conv2"); }
+        else if (b.kind != BlockKind::Xfmr) out.insert(b.name);
+    }
+    return out;
+}
+
+// Device layout of one linear (src/engine.cu:20-46 describes the same layout): W rows padded to Np = 64k output
+// channels and Kp = 16k inputs, zeros in the padding; a 3x3 kernel, stored with input index c*9 + tap, is re-ordered so
+// that input (ky*3+kx)*C + c follows tap by tap (an implicit-GEMM K block then reads 32 channels of one tap); per
+// output channel the constants {m, s, b, sum of the channel's weights}, and {1, 0, 0, 0} for padding channels.
+static HostLin pack_linear(const Poisd& f, const std::string& base, const PoisdEntry& wt, bool kernel3x3) {
+    HostLin h;
+    h.N = int(wt.dims[0]); h.K = int(wt.dims[1]); h.conv3 = kernel3x3;
+    h.Np = int(align_up(h.N, 64)); h.Kp = int(align_up(h.K, 16));
+    if (kernel3x3 && h.K % 9 != 0) throw Error(VELA_ERR_IO, "3x3 kernel " + base + " has " + std::to_string(h.K) + " inputs, not 9 per channel");
+    const int chans = kernel3x3 ? h.K / 9 : h.K;
+    const int8_t* src = f.i8(base + ".w");
+    const std::vector<int32_t> mul = f.i32(base + ".m"), shift = f.i32(base + ".s"), bias = f.i32(base + ".b");
+    if (int(mul.size()) != h.N || int(shift.size()) != h.N || int(bias.size()) != h.N) throw Error(VELA_ERR_IO, base + ": per-channel constants do not match its rows");
+    h.w.assign(size_t(h.Np) * h.Kp, 0);
+    h.cst.assign(size_t(h.Np) * 4, 0);
+    for (int o = 0; o < h.Np; ++o) {
+        int32_t* cc = &h.cst[4 * size_t(o)];
+        if (o >= h.N) { cc[0] = 1; continue; }
+        const int8_t* in = src + size_t(o) * h.K;
+        int8_t* row = &h.w[size_t(o) * h.Kp];
+        if (kernel3x3) {
+            for (int tap = 0; tap < 9; ++tap)
+                for (int c = 0; c < chans; ++c) row[size_t(tap) * chans + c] = in[size_t(c) * 9 + tap];
+        } else {
+            std::memcpy(row, in, size_t(h.K));
+        }
+        int32_t acc = 0;
+        for (int k = 0; k < h.K; ++k) acc += in[k];
+        cc[0] = mul[o]; cc[1] = shift[o]; cc[2] = bias[o]; cc[3] = acc;
+    }
+    return h;
+}
 
 class Model {
 public:
@@ -98,27 +196,14 @@ public:
         VELA_CUDA(cudaSetDevice(dev));
         Poisd f; f.load(path);
         std::map<std::string, HostLin> hl;
-        // linears: <base>.w int8 [N, K] with <base>.m/.s/.b (src/engine.cu:20-46)
+        // every linear the file holds: <base>.w int8 [N, K] with per-channel <base>.m / .s / .b
+        const std::set<std::string> k3 = kernel3x3_names();
         for (const auto& kv : f.entries()) {
-            const std::string& name = kv.first; const PoisdEntry& t = kv.second;
-            if (t.dtype != 0 || !ends(name, ".w") || t.dims.size() != 2) continue;
+            const std::string& name = kv.first;
+            if (kv.second.dtype != 0 || kv.second.dims.size() != 2 || name.size() < 3 || name.compare(name.size() - 2, 2, ".w") != 0) continue;
             const std::string base = name.substr(0, name.size() - 2);
-            if (base == "te.tok" || !f.has(base + ".m")) continue;
-            HostLin L; L.N = int(t.dims[0]); L.K = int(t.dims[1]); L.Np = int(align_up(L.N, 64)); L.Kp = int(align_up(L.K, 16));
-            L.conv3 = ends(base, ".conv1") || ends(base, ".conv2") || ends(base, "conv_in") || ends(base, "conv_out") ||
-                      ends(base, "downsamplers.0.conv") || ends(base, "upsamplers.0.conv");
-            const int C = L.conv3 ? L.K / 9 : 0;
-            if (L.conv3 && C * 9 != L.K) throw Error(VELA_ERR_IO, "conv weight K not a multiple of 9: " + name);
-            const int8_t* w = f.i8(name);
-            const auto m = f.i32(base + ".m"), s = f.i32(base + ".s"), b = f.i32(base + ".b");
-            L.w.assign(size_t(L.Np) * L.Kp, 0); L.cst.assign(size_t(L.Np) * 4, 0);
-            for (int n = L.N; n < L.Np; ++n) L.cst[4 * size_t(n)] = 1;
-            for (int n = 0; n < L.N; ++n) {
-                const int8_t* row = w + size_t(n) * L.K; int8_t* dst = L.w.data() + size_t(n) * L.Kp; i64 sum = 0;
-                for (int k = 0; k < L.K; ++k) { const int kk = L.conv3 ? (k % 9) * C + k / 9 : k; dst[kk] = row[k]; sum += row[k]; }   // tap-major K for 3x3
-                L.cst[4 * size_t(n)] = m[n]; L.cst[4 * size_t(n) + 1] = s[n]; L.cst[4 * size_t(n) + 2] = b[n]; L.cst[4 * size_t(n) + 3] = int32_t(sum);
-            }
-            hl.emplace(base, std::move(L));
+            if (base == "te.tok" || !f.has(base + ".m")) continue;          // the token table is an embedding, not a linear
+            hl.emplace(base, pack_linear(f, base, kv.second, k3.count(base) != 0));
         }
         // merged projections (src/engine.cu:63-101): q|k|v rows, GEGLU a|g interleaved
         auto merge = [&](const std::string& name, const std::vector<std::string>& parts, bool interleave) {
@@ -142,8 +227,9 @@ public:
             }
             hl.emplace(name, std::move(L));
         };
-        for (int i = 0; i < 16; ++i) {
-            const std::string b = block_name(i) + ".transformer_blocks.0";
+        for (const UNetBlock& blk : unet_plan()) {
+            if (blk.kind != BlockKind::Xfmr) continue;
+            const std::string b = inner_block(blk);
             merge(b + ".attn1.to_qkv", {b + ".attn1.to_q", b + ".attn1.to_k", b + ".attn1.to_v"}, false);
             merge(b + ".ff.net.0.proj.agi", {b + ".ff.net.0.proj.a", b + ".ff.net.0.proj.g"}, true);
         }
@@ -161,7 +247,7 @@ public:
         // norms: <base>.g / .beta / .eps (src/engine.cu:47-56)
         for (const auto& kv : f.entries()) {
             const std::string& name = kv.first;
-            if (!ends(name, ".g")) continue;
+            if (!ends_with(name, ".g")) continue;
             const std::string base = name.substr(0, name.size() - 2);
             if (!f.has(base + ".beta") || !f.has(base + ".eps")) continue;
             const auto g = f.i32(name), bt = f.i32(base + ".beta");
@@ -183,13 +269,6 @@ public:
         tok_m = up64("te.tok.m"); tok_s = up64("te.tok.s"); te_pos = up64("te.pos");
         VELA_CUDA(cudaDeviceSynchronize());
     }
-    static std::string block_name(int idx) {       // the 16 transformer blocks in UNet order
-        if (idx < 6) return "unet.down_blocks." + std::to_string(idx / 2) + ".attentions." + std::to_string(idx % 2);
-        if (idx == 6) return "unet.mid_block.attentions.0";
-        const int i = 1 + (idx - 7) / 3, j = (idx - 7) % 3;
-        return "unet.up_blocks." + std::to_string(i) + ".attentions." + std::to_string(j);
-    }
-    static int block_heads(int idx) { static const int H[4] = {5, 10, 20, 20}; return idx < 6 ? H[idx / 2] : (idx == 6 ? 20 : H[3 - (1 + (idx - 7) / 3)]); }
 private:
     std::vector<void*> allocs_;
     void* upload(const void* src, size_t n) {
@@ -232,6 +311,7 @@ public:
         dNoise_ = static_cast<int32_t*>(palloc(size_t(B_) * 16384 * 4)); dX_ = static_cast<int32_t*>(palloc(size_t(B_) * 16384 * 4));
         dEps_ = static_cast<int32_t*>(palloc(size_t(B_) * 16384 * 4)); dIds_ = static_cast<int32_t*>(palloc(128 * 4));
         dCtx_ = static_cast<int32_t*>(palloc(size_t(77) * m.te_dim * 4));
+        for (const UNetBlock& b : unet_plan()) if (b.kind == BlockKind::Xfmr) cross_.resize(std::max(cross_.size(), size_t(b.xattn) + 1));
         VELA_CUDA(cudaEventCreate(&ev0_)); VELA_CUDA(cudaEventCreateWithFlags(&ev1_, cudaEventBlockingSync));
         // this engine's own device error word: its kernels report a timed-out wait here, and each step copies it out
         // beside x0, so collect / run fail with VELA_ERR_TIMEOUT for exactly the steps that timed out
@@ -276,14 +356,15 @@ public:
         text_encoder(ids);
         const int T = 77, D = m_.te_dim;
         Tensor ctx; ctx.d = dCtx_; ctx.B = 1; ctx.T = T; ctx.C = D;
-        for (int i = 0; i < 16; ++i) {
-            const std::string b = Model::block_name(i) + ".transformer_blocks.0";
-            const int heads = Model::block_heads(i);
+        for (const UNetBlock& blk : unet_plan()) {
+            if (blk.kind != BlockKind::Xfmr) continue;
+            const std::string b = inner_block(blk);
+            const int heads = blk.heads, i = blk.xattn;
             const size_t mk = arena_.off;
             Tensor k = lin_x(ctx, m_.lin(b + ".attn2.to_k")), v = lin_x(ctx, m_.lin(b + ".attn2.to_v"));
             const int C = k.C, G1 = heads, Tkp = 128;
             VELA_REQUIRE(C == heads * 64, "cross-attention width");
-            KV& kv = cross_[i];
+            KV& kv = cross_.at(size_t(i));
             if (!kv.khi) {
                 kv.Tk = T; kv.Tkp = Tkp;
                 const size_t G = size_t(B_) * G1;
@@ -404,7 +485,7 @@ private:
     int inflight_ = 0, sub_slot_ = 0, col_slot_ = 0;
     int32_t *dNoise_ = nullptr, *dX_ = nullptr, *dEps_ = nullptr, *dIds_ = nullptr, *dCtx_ = nullptr;
     unsigned* dErr_ = nullptr; unsigned* hErr_[2] = {nullptr, nullptr}; LaunchOpts lo_;
-    KV cross_[16];
+    std::vector<KV> cross_;                   // per transformer block of the plan: the prompt's cross-attention K/V
     bool have_prompt_ = false;
     TapFn tap_ = nullptr; void* tap_user_ = nullptr;
     static constexpr size_t WORKSPACE = size_t(64) << 20;    // split-K partials
@@ -576,109 +657,108 @@ private:
                         q.B, heads, Tq, q.Tp, kv.Tk, kv.Tkp, causal, m_.lut_exp, C, out.d, out.rowmax, lo_);
         return out;
     }
-    // Engine::resnet (src/engine.cu:389-405)
-    Tensor resnet(const Tensor& x, int H, int W, const std::string& p) {
-        const Lin& c1 = m_.lin(p + ".conv1"); const Lin& c2 = m_.lin(p + ".conv2");
-        Tensor out = talloc(x.B, x.T, c2.N);
-        const size_t mk = arena_.off;
-        uint32_t *pm1 = nullptr, *pm2 = nullptr;
-        Tensor h = gn_silu(x, m_.norm(p + ".norm1"), pm1);
-        Tensor h1 = conv3(h, H, W, c1, 1, nullptr, nullptr, pm1);
-        Tensor h2 = gn_silu(h1, m_.norm(p + ".norm2"), pm2);
-        if (m_.has_lin(p + ".conv_shortcut")) { Tensor xs = lin_x(x, m_.lin(p + ".conv_shortcut")); conv3(h2, H, W, c2, 1, out.d, xs.d, pm2); }
-        else conv3(h2, H, W, c2, 1, out.d, x.d, pm2);
-        arena_.off = mk;
-        return out;
+    // GroupNorm + SiLU of x, then a 3x3 convolution of the result (stride 1) into `out` (+ residual): the resnet's two
+    // halves and the output head; the normalised tensor's pixel maxima feed the convolution's window exponents
+    Tensor norm_act_conv(const Tensor& x, int side, const Norm& norm, const Lin& conv, int32_t* out = nullptr, const int32_t* residual = nullptr) {
+        Tensor y; y.B = x.B; y.T = x.T; y.C = conv.N;
+        y.d = out ? out : static_cast<int32_t*>(arena_.alloc(y.n() * 4));
+        const size_t scope = arena_.off;
+        uint32_t* pix = nullptr;
+        const Tensor act = gn_silu(x, norm, pix);
+        conv3(act, side, side, conv, 1, y.d, residual, pix);
+        arena_.off = scope;
+        return y;
     }
-    // Engine::transformer (src/engine.cu:406-454)
-    Tensor transformer(const Tensor& x, const std::string& p, int heads, int blockIdx) {
-        const int B = x.B, T = x.T, C = x.C;
-        Tensor out = talloc(B, T, C);
-        const size_t mk = arena_.off;
-        const std::string b = p + ".transformer_blocks.0";
-        Tensor h = talloc(B, T, C);
-        h.rowmax = rowmax_alloc(B * T);          // row max of h after the feed-forward (consumed by proj_out)
-        { const size_t m2 = arena_.off; QIn xq = gn_q(x, m_.norm(p + ".norm")); lin_q(xq, m_.lin(p + ".proj_in"), h.d); arena_.off = m2; }
-        {
-            const size_t m2 = arena_.off;
-            QIn n = ln_q(h, m_.norm(b + ".norm1"));
-            HeadQ qh, kh; Tensor v;
-            qkv(n, m_.lin(b + ".attn1.to_qkv"), C, heads, T, qh, kh, v);
-            KV kv = kv_of(kh, v, heads);
-            Tensor a = attention(qh, kv, heads, false, T, C);
-            lin_x(a, m_.lin(b + ".attn1.to_out.0"), h.d, h.d);
-            arena_.off = m2;
-        }
-        {
-            const size_t m2 = arena_.off;
-            QIn n = ln_q(h, m_.norm(b + ".norm2"));
-            HeadQ qh = q_only(n, m_.lin(b + ".attn2.to_q"), C, heads, T);
-            Tensor a = attention(qh, cross_[blockIdx], heads, false, T, C);
-            lin_x(a, m_.lin(b + ".attn2.to_out.0"), h.d, h.d);
-            arena_.off = m2;
-        }
-        {
-            const size_t m2 = arena_.off;
-            QIn n = ln_q(h, m_.norm(b + ".norm3"));
-            const Lin& Li = m_.lin(b + ".ff.net.0.proj.agi");
-            const int F = Li.N / 2;
-            Tensor v; v.B = B; v.T = T; v.C = F; v.d = static_cast<int32_t*>(arena_.alloc(v.n() * 4)); v.rowmax = rowmax_alloc(B * T);
-            vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n.hi; A.lo = n.lo; A.ld8 = n.Kp; A.e = n.e;
-            vela_aepi E; std::memset(&E, 0, sizeof(E)); E.epi = VELA_EPI_GEGLU; E.Y = v.d; E.ldy = F; E.Lphi = m_.lut_phi; E.rowmax = v.rowmax;
-            gemm_w8a16(st_, A, n.Mp, n.rows(), Li.w, Li.Kp, Li.Np, Li.N, Li.Kp, Li.cst, E, lo_);
-            const Lin& L2 = m_.lin(b + ".ff.net.2");
-            VELA_REQUIRE(L2.K == F, "ff.net.2: K mismatch");
-            gemm_x(v.d, B * T, F, v.rowmax, L2, epi_plain(h.d, C, h.d, h.rowmax));
-            arena_.off = m2;
-        }
-        lin_x(h, m_.lin(p + ".proj_out"), out.d, x.d);
-        arena_.off = mk;
-        return out;
+    // resnet block (src/engine.cu:389-405 computes the same): two norm-act-conv halves, the second one adding the
+    // shortcut -- the input itself, or its 1x1 projection when the width changes
+    Tensor res_block(const Tensor& x, int side, const std::string& p) {
+        const Lin& second = m_.lin(p + ".conv2");
+        Tensor y = talloc(x.B, x.T, second.N);
+        const size_t scope = arena_.off;
+        const Tensor mid = norm_act_conv(x, side, m_.norm(p + ".norm1"), m_.lin(p + ".conv1"));
+        const int32_t* shortcut = m_.has_lin(p + ".conv_shortcut") ? lin_x(x, m_.lin(p + ".conv_shortcut")).d : x.d;
+        norm_act_conv(mid, side, m_.norm(p + ".norm2"), second, y.d, shortcut);
+        arena_.off = scope;
+        return y;
     }
-    // Engine::unet (src/engine.cu:455-490)
+    // the three residual sub-layers of a transformer block, each adding into the running rows h (rows of x, width C)
+    void self_attention_into(Tensor& h, const std::string& b, int heads) {
+        const QIn n = ln_q(h, m_.norm(b + ".norm1"));
+        HeadQ q, k; Tensor v;
+        qkv(n, m_.lin(b + ".attn1.to_qkv"), h.C, heads, h.T, q, k, v);
+        const Tensor o = attention(q, kv_of(k, v, heads), heads, false, h.T, h.C);
+        lin_x(o, m_.lin(b + ".attn1.to_out.0"), h.d, h.d);
+    }
+    void cross_attention_into(Tensor& h, const std::string& b, int heads, const KV& prompt) {
+        const QIn n = ln_q(h, m_.norm(b + ".norm2"));
+        const Tensor o = attention(q_only(n, m_.lin(b + ".attn2.to_q"), h.C, heads, h.T), prompt, heads, false, h.T, h.C);
+        lin_x(o, m_.lin(b + ".attn2.to_out.0"), h.d, h.d);
+    }
+    // GEGLU feed-forward; its second GEMM also leaves the row maxima of h for proj_out's quantise-on-load
+    void feed_forward_into(Tensor& h, const std::string& b) {
+        const QIn n = ln_q(h, m_.norm(b + ".norm3"));
+        const Lin& up = m_.lin(b + ".ff.net.0.proj.agi");
+        Tensor g; g.B = h.B; g.T = h.T; g.C = up.N / 2;
+        g.d = static_cast<int32_t*>(arena_.alloc(g.n() * 4)); g.rowmax = rowmax_alloc(h.B * h.T);
+        vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = n.hi; A.lo = n.lo; A.ld8 = n.Kp; A.e = n.e;
+        vela_aepi E; std::memset(&E, 0, sizeof(E)); E.epi = VELA_EPI_GEGLU; E.Y = g.d; E.ldy = g.C; E.Lphi = m_.lut_phi; E.rowmax = g.rowmax;
+        gemm_w8a16(st_, A, n.Mp, n.rows(), up.w, up.Kp, up.Np, up.N, up.Kp, up.cst, E, lo_);
+        const Lin& down = m_.lin(b + ".ff.net.2");
+        VELA_REQUIRE(down.K == g.C, "ff.net.2: input width differs from the GEGLU output");
+        gemm_x(g.d, h.B * h.T, g.C, g.rowmax, down, epi_plain(h.d, h.C, h.d, h.rowmax));
+    }
+    // transformer block (src/engine.cu:406-454 computes the same): GroupNorm -> proj_in -> the three sub-layers on
+    // the rows h -> proj_out + the block input
+    Tensor transformer(const Tensor& x, const UNetBlock& blk) {
+        Tensor y = talloc(x.B, x.T, x.C);
+        const size_t scope = arena_.off;
+        Tensor h = talloc(x.B, x.T, x.C);
+        h.rowmax = rowmax_alloc(x.B * x.T);
+        const std::string b = inner_block(blk);
+        auto sublayer = [&](auto&& body) { const size_t m = arena_.off; body(); arena_.off = m; };
+        sublayer([&] { lin_q(gn_q(x, m_.norm(blk.name + ".norm")), m_.lin(blk.name + ".proj_in"), h.d); });
+        sublayer([&] { self_attention_into(h, b, blk.heads); });
+        sublayer([&] { cross_attention_into(h, b, blk.heads, cross_.at(size_t(blk.xattn))); });
+        sublayer([&] { feed_forward_into(h, b); });
+        lin_x(h, m_.lin(blk.name + ".proj_out"), y.d, x.d);
+        arena_.off = scope;
+        return y;
+    }
+    // the UNet (src/engine.cu:455-490): the block table walked in order; kept results live until their resnet on the
+    // way up consumes them
     void unet(const Tensor& x, Tensor& eps) {
-        static const int HEADS[4] = {5, 10, 20, 20};
-        int H = 64, W = 64;
-        Tensor h = conv3(x, H, W, m_.lin("unet.conv_in"), 1);
-        emit("conv_in", h);
-        std::vector<Tensor> skips; skips.push_back(h);
-        int blk = 0;
-        for (int i = 0; i < 4; ++i) {
-            for (int j = 0; j < 2; ++j) {
-                std::string n = "unet.down_blocks." + std::to_string(i) + ".resnets." + std::to_string(j);
-                h = resnet(h, H, W, n); emit(n, h);
-                if (i < 3) { n = "unet.down_blocks." + std::to_string(i) + ".attentions." + std::to_string(j); h = transformer(h, n, HEADS[i], blk++); emit(n, h); }
-                skips.push_back(h);
+        int side = 64;
+        Tensor h = x;
+        std::vector<Tensor> kept;
+        for (const UNetBlock& blk : unet_plan()) {
+            switch (blk.kind) {
+                case BlockKind::ConvIn: h = conv3(h, side, side, m_.lin(blk.name), 1); break;
+                case BlockKind::Res:
+                    if (blk.pop) {
+                        VELA_REQUIRE(!kept.empty(), "unet: no kept tensor for " + blk.name);
+                        const Tensor s = kept.back(); kept.pop_back();
+                        Tensor cat = talloc(h.B, h.T, h.C + s.C);
+                        concat(st_, h.d, h.C, s.d, s.C, h.B * h.T, cat.d);
+                        h = cat;
+                    }
+                    h = res_block(h, side, blk.name);
+                    break;
+                case BlockKind::Xfmr: h = transformer(h, blk); break;
+                case BlockKind::Down: h = conv3(h, side, side, m_.lin(blk.name), 2); side /= 2; break;
+                case BlockKind::Up: {
+                    Tensor up = talloc(h.B, h.T * 4, h.C);
+                    upsample2(st_, h.d, h.B, side, side, h.C, up.d);
+                    side *= 2;
+                    h = conv3(up, side, side, m_.lin(blk.name), 1);
+                    break;
+                }
+                case BlockKind::Out:
+                    h = norm_act_conv(h, side, m_.norm("unet.conv_norm_out"), m_.lin(blk.name), eps.d);
+                    break;
             }
-            if (i < 3) {
-                const std::string n = "unet.down_blocks." + std::to_string(i) + ".downsamplers.0.conv";
-                h = conv3(h, H, W, m_.lin(n), 2); emit(n, h);
-                H /= 2; W /= 2; skips.push_back(h);
-            }
+            if (blk.push) kept.push_back(h);
+            emit(blk.tap, h);
         }
-        h = resnet(h, H, W, "unet.mid_block.resnets.0"); emit("unet.mid_block.resnets.0", h);
-        h = transformer(h, "unet.mid_block.attentions.0", 20, blk++); emit("unet.mid_block.attentions.0", h);
-        h = resnet(h, H, W, "unet.mid_block.resnets.1"); emit("unet.mid_block.resnets.1", h);
-        for (int i = 0; i < 4; ++i) {
-            for (int j = 0; j < 3; ++j) {
-                const Tensor s = skips.back(); skips.pop_back();
-                Tensor c = talloc(h.B, h.T, h.C + s.C);
-                concat(st_, h.d, h.C, s.d, s.C, h.B * h.T, c.d);
-                std::string n = "unet.up_blocks." + std::to_string(i) + ".resnets." + std::to_string(j);
-                h = resnet(c, H, W, n); emit(n, h);
-                if (i > 0) { n = "unet.up_blocks." + std::to_string(i) + ".attentions." + std::to_string(j); h = transformer(h, n, HEADS[3 - i], blk++); emit(n, h); }
-            }
-            if (i < 3) {
-                Tensor u = talloc(h.B, h.T * 4, h.C);
-                upsample2(st_, h.d, h.B, H, W, h.C, u.d); H *= 2; W *= 2;
-                const std::string n = "unet.up_blocks." + std::to_string(i) + ".upsamplers.0.conv";
-                h = conv3(u, H, W, m_.lin(n), 1); emit(n, h);
-            }
-        }
-        uint32_t* pmo = nullptr;
-        Tensor nrm = gn_silu(h, m_.norm("unet.conv_norm_out"), pmo);
-        conv3(nrm, H, W, m_.lin("unet.conv_out"), 1, eps.d, nullptr, pmo);
-        emit("eps", eps);
     }
     // Engine::textEncoder (src/engine.cu:491-527), the 77 real rows
     void text_encoder(const std::vector<int32_t>& ids) {

@@ -481,59 +481,110 @@ __global__ void upsample2_kernel(const int32_t* __restrict__ X, int B, int H, in
 }
 
 // ---------------------------------------------------------------- ChaCha20 noise and finalize (src/kernels.cu:563-599)
-__device__ __forceinline__ u32 rotl(u32 v, int n) { return __funnelshift_l(v, v, n); }
-#define VELA_QR(a, b, c, d) a += b; d ^= a; d = rotl(d, 16); c += d; b ^= c; b = rotl(b, 12); a += b; d ^= a; d = rotl(d, 8); c += d; b ^= c; b = rotl(b, 7);
-// thread = one 64-byte keystream block (RFC 7539 block function, counter = block index, nonce 0) of one sample
-__global__ void noise_kernel(const uint8_t* __restrict__ seeds, int B, const i64* __restrict__ gauss64, const int32_t* __restrict__ gauss32, i64 cin,
-                             int32_t* __restrict__ n, int32_t* __restrict__ x) {
-    const int blk = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
-    if (blk >= 512 || b >= B) return;
-    const uint8_t* key = seeds + 32 * b;
-    u32 in[16], st[16];
-    in[0] = 0x61707865u; in[1] = 0x3320646eu; in[2] = 0x79622d32u; in[3] = 0x6b206574u;
+// ChaCha20 block function (RFC 7539 section 2.3): 16-word state = 4 constant words, the 8 key words, block counter,
+// 3 nonce words (zero here); 10 double rounds, each a column round and a diagonal round of quarter rounds; output
+// word i = round state i + initial state i.
+__device__ __forceinline__ void chacha_qround(u32& a, u32& b, u32& c, u32& d) {
+    a += b; d = __funnelshift_l(d ^ a, d ^ a, 16);
+    c += d; b = __funnelshift_l(b ^ c, b ^ c, 12);
+    a += b; d = __funnelshift_l(d ^ a, d ^ a, 8);
+    c += d; b = __funnelshift_l(b ^ c, b ^ c, 7);
+}
+__device__ __forceinline__ void chacha20_block(const u32* key, u32 counter, u32 (&out)[16]) {
+    u32 x[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u, key[0], key[1], key[2], key[3],
+                 key[4], key[5], key[6], key[7], counter, 0u, 0u, 0u};
     #pragma unroll
-    for (int i = 0; i < 8; ++i) in[4 + i] = u32(key[4 * i]) | (u32(key[4 * i + 1]) << 8) | (u32(key[4 * i + 2]) << 16) | (u32(key[4 * i + 3]) << 24);
-    in[12] = u32(blk); in[13] = 0; in[14] = 0; in[15] = 0;
+    for (int i = 0; i < 16; ++i) out[i] = x[i];
     #pragma unroll
-    for (int i = 0; i < 16; ++i) st[i] = in[i];
-    #pragma unroll
-    for (int r = 0; r < 10; ++r) {
-        VELA_QR(st[0], st[4], st[8], st[12]) VELA_QR(st[1], st[5], st[9], st[13]) VELA_QR(st[2], st[6], st[10], st[14]) VELA_QR(st[3], st[7], st[11], st[15])
-        VELA_QR(st[0], st[5], st[10], st[15]) VELA_QR(st[1], st[6], st[11], st[12]) VELA_QR(st[2], st[7], st[8], st[13]) VELA_QR(st[3], st[4], st[9], st[14])
+    for (int dr = 0; dr < 10; ++dr) {
+        #pragma unroll
+        for (int col = 0; col < 4; ++col) chacha_qround(x[col], x[4 + col], x[8 + col], x[12 + col]);
+        #pragma unroll
+        for (int dg = 0; dg < 4; ++dg) chacha_qround(x[dg], x[4 + (dg + 1) % 4], x[8 + (dg + 2) % 4], x[12 + (dg + 3) % 4]);
     }
-    int32_t* nb = n + size_t(b) * 16384; int32_t* xb = x + size_t(b) * 16384;
-    int nv[32];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] += x[i];
+}
+// Noise of one sample: 16384 values, value v = gauss[u16 v of the keystream] (little-endian halves of the output
+// words, block k holding values 32k .. 32k+31), stored channel-major n[c][p] (v = 4096 c + p), and the scaled latent
+// x[p][c] = rshr(n[c][p] cin, 30) in NHWC.  CTA = (a quarter of the 4096 pixels, one sample), 128 threads: thread t
+// makes block 128 (t / 32) + 32 quarter + t % 32 -- 32 pixels of channel t / 32 -- writes them to n and to shared
+// memory, then the CTA writes its 1024 NHWC pixels as one 16-byte store each.
+__global__ void __launch_bounds__(128) noise_kernel(const uint8_t* __restrict__ seeds, const i64* __restrict__ gauss64,
+                                                    const int32_t* __restrict__ gauss32, i64 cin, int32_t* __restrict__ n, int32_t* __restrict__ x) {
+    __shared__ u32 key[8];
+    __shared__ int32_t ns[4][1024];
+    const int quarter = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    if (t < 8) {
+        const uint8_t* kp = seeds + 32 * size_t(b) + 4 * t;
+        key[t] = u32(kp[0]) | (u32(kp[1]) << 8) | (u32(kp[2]) << 16) | (u32(kp[3]) << 24);
+    }
+    __syncthreads();
+    const int c = t >> 5, j = quarter * 32 + (t & 31);          // channel, block within the channel (0..127)
+    u32 ks[16];
+    chacha20_block(key, u32(c * 128 + j), ks);
+    int v[32];
     #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const u32 w = st[i] + in[i];
-        nv[2 * i] = gauss32 ? __ldg(gauss32 + (w & 0xffffu)) : int(gauss64[w & 0xffffu]);
-        nv[2 * i + 1] = gauss32 ? __ldg(gauss32 + (w >> 16)) : int(gauss64[w >> 16]);
+        const u32 lo16 = ks[i] & 0xffffu, hi16 = ks[i] >> 16;
+        v[2 * i] = gauss32 ? __ldg(gauss32 + lo16) : int(__ldg(gauss64 + lo16));
+        v[2 * i + 1] = gauss32 ? __ldg(gauss32 + hi16) : int(__ldg(gauss64 + hi16));
     }
+    int4* nout = reinterpret_cast<int4*>(n + size_t(b) * 16384 + c * 4096 + j * 32);
     #pragma unroll
-    for (int i = 0; i < 32; i += 4) *reinterpret_cast<int4*>(nb + blk * 32 + i) = make_int4(nv[i], nv[i + 1], nv[i + 2], nv[i + 3]);
-    // all 32 values of this block share the channel (idx >> 12): channel-major n, NHWC x
+    for (int i = 0; i < 8; ++i) nout[i] = make_int4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int idx = blk * 32 + i;
-        xb[(idx & 4095) * 4 + (idx >> 12)] = int(rshr(i64(nv[i]) * cin, 30));
+    for (int i = 0; i < 32; ++i) ns[c][(t & 31) * 32 + i] = v[i];
+    __syncthreads();
+    int4* xout = reinterpret_cast<int4*>(x + size_t(b) * 16384) + quarter * 1024;
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int p = t + 128 * k;
+        xout[p] = make_int4(int(rshr(i64(ns[0][p]) * cin, 30)), int(rshr(i64(ns[1][p]) * cin, 30)),
+                            int(rshr(i64(ns[2][p]) * cin, 30)), int(rshr(i64(ns[3][p]) * cin, 30)));
     }
 }
-__global__ void finalize_kernel(const int32_t* __restrict__ n, const int32_t* __restrict__ eps, int B, i64 sig, uint8_t* __restrict__ out) {
-    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= size_t(B) * 16384) return;
-    const int b = int(i / 16384), idx = int(i % 16384), c = idx >> 12, p = idx & 4095;
-    const i64 x0 = rshr((i64(n[i]) - eps[size_t(b) * 16384 + p * 4 + c]) * sig, 16);
-    const i64 q = min(max(rshr(x0, 8), i64(-32767)), i64(32767));
-    reinterpret_cast<uint16_t*>(out)[i] = uint16_t(int16_t(q));      // little-endian int16
+// x0 = rshr((n - eps) sig, 16), out = clamp(rshr(x0, 8), +-32767) as little-endian int16 in n's channel-major order;
+// eps is NHWC.  Thread = two neighbouring pixels of one sample: eps as two 16-byte loads, n as one 8-byte load per
+// channel, the output as one packed pair of int16 per channel.
+__global__ void finalize_kernel(const int32_t* __restrict__ n, const int32_t* __restrict__ eps, int B, i64 sig, uint32_t* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * 2048) return;
+    const int b = i >> 11, p = (i & 2047) * 2;
+    const int4 e0 = __ldg(reinterpret_cast<const int4*>(eps + size_t(b) * 16384 + p * 4));
+    const int4 e1 = __ldg(reinterpret_cast<const int4*>(eps + size_t(b) * 16384 + p * 4 + 4));
+    const int ea[4] = {e0.x, e0.y, e0.z, e0.w}, eb[4] = {e1.x, e1.y, e1.z, e1.w};
+    auto q16 = [&](int nv, int ev) -> uint32_t {
+        const i64 x0 = rshr((i64(nv) - ev) * sig, 16);
+        return uint32_t(uint16_t(int16_t(min(max(rshr(x0, 8), i64(-32767)), i64(32767)))));
+    };
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const size_t at = size_t(b) * 16384 + c * 4096 + p;
+        const int2 nv = __ldg(reinterpret_cast<const int2*>(n + at));
+        out[at >> 1] = q16(nv.x, ea[c]) | (q16(nv.y, eb[c]) << 16);
+    }
 }
-__global__ void text_embed_kernel(const int32_t* __restrict__ ids, int T, int rowsPad, const int8_t* __restrict__ tw, const i64* __restrict__ tm,
+// token embedding of the prompt rows: X[t][d] = sat32(rshr(w[id][d] m[id], s[id] - 16) + pos[t][d]) for t < T, 0 for
+// the padding rows.  CTA = one row; thread = four neighbouring d (4-byte weight loads, 16-byte stores).
+__global__ void text_embed_kernel(const int32_t* __restrict__ ids, int T, const int8_t* __restrict__ tw, const i64* __restrict__ tm,
                                   const i64* __restrict__ ts, const i64* __restrict__ pos, int D, int32_t* __restrict__ X) {
-    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= size_t(rowsPad) * D) return;
-    const int t = int(i / D), d = int(i % D);
-    if (t >= T) { X[i] = 0; return; }
-    const int id = ids[t];
-    X[i] = int(sat32(rshr(i64(tw[size_t(id) * D + d]) * tm[id], ts[id] - 16) + pos[size_t(t) * D + d]));
+    const int t = blockIdx.x;
+    int4* row = reinterpret_cast<int4*>(X + size_t(t) * D);
+    if (t >= T) {
+        for (int d4 = threadIdx.x; d4 < D / 4; d4 += blockDim.x) row[d4] = make_int4(0, 0, 0, 0);
+        return;
+    }
+    const int id = __ldg(ids + t);
+    const i64 m = __ldg(tm + id), sh = __ldg(ts + id) - 16;
+    const char4* w = reinterpret_cast<const char4*>(tw + size_t(id) * D);
+    const longlong2* ps = reinterpret_cast<const longlong2*>(pos + size_t(t) * D);
+    for (int d4 = threadIdx.x; d4 < D / 4; d4 += blockDim.x) {
+        const char4 wv = __ldg(w + d4);
+        const longlong2 p01 = __ldg(ps + 2 * d4), p23 = __ldg(ps + 2 * d4 + 1);
+        row[d4] = make_int4(int(sat32(rshr(i64(wv.x) * m, sh) + p01.x)), int(sat32(rshr(i64(wv.y) * m, sh) + p01.y)),
+                            int(sat32(rshr(i64(wv.z) * m, sh) + p23.x)), int(sat32(rshr(i64(wv.w) * m, sh) + p23.y)));
+    }
 }
 
 // ---------------------------------------------------------------- attention operands (src/kernels.cu:609-669,799-809)
@@ -688,15 +739,20 @@ void upsample2(cudaStream_t st, const int32_t* X, int B, int H, int W, int C, in
 }
 void noise(cudaStream_t st, const uint8_t* seeds, int B, const i64* gauss64, const int32_t* gauss32, i64 cin, int32_t* n, int32_t* x) {
     VELA_REQUIRE(seeds && (gauss64 || gauss32) && n && x && B > 0, "noise: bad arguments");
-    noise_kernel<<<dim3(4, B), 128, 0, st>>>(seeds, B, gauss64, gauss32, cin, n, x);
+    VELA_REQUIRE((reinterpret_cast<uintptr_t>(n) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0, "noise: n and x must be 16-byte aligned");
+    noise_kernel<<<dim3(4, B), 128, 0, st>>>(seeds, gauss64, gauss32, cin, n, x);
 }
 void finalize(cudaStream_t st, const int32_t* n, const int32_t* eps, int B, i64 sig, uint8_t* out) {
     VELA_REQUIRE(n && eps && out && B > 0, "finalize: bad arguments");
-    finalize_kernel<<<ceil_div(B * 16384, 256), 256, 0, st>>>(n, eps, B, sig, out);
+    VELA_REQUIRE((reinterpret_cast<uintptr_t>(n) & 7) == 0 && (reinterpret_cast<uintptr_t>(eps) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0,
+                 "finalize: n must be 8-byte, eps 16-byte and out 4-byte aligned");
+    finalize_kernel<<<ceil_div(B * 2048, 256), 256, 0, st>>>(n, eps, B, sig, reinterpret_cast<uint32_t*>(out));
 }
 void text_embed(cudaStream_t st, const int32_t* ids, int T, int rowsPad, const int8_t* tw, const i64* tm, const i64* ts, const i64* pos, int D, int32_t* X) {
     VELA_REQUIRE(ids && tw && tm && ts && pos && X, "text_embed: bad arguments");
-    text_embed_kernel<<<ceil_div(rowsPad * D, 256), 256, 0, st>>>(ids, T, rowsPad, tw, tm, ts, pos, D, X);
+    VELA_REQUIRE(D % 4 == 0 && rowsPad >= T && T >= 0 && (reinterpret_cast<uintptr_t>(tw) & 3) == 0 && (reinterpret_cast<uintptr_t>(pos) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(X) & 15) == 0, "text_embed: D % 4 == 0, rowsPad >= T, aligned tw / pos / X");
+    if (rowsPad > 0) text_embed_kernel<<<rowsPad, 256, 0, st>>>(ids, T, tw, tm, ts, pos, D, X);
 }
 void quant_heads(cudaStream_t st, const int32_t* X, int B, int T, int C, int heads, int Tp, int8_t* hi, int8_t* lo, int32_t* e, i64* hs, i64* ls, i64* tsum, int tFrom) {
     VELA_REQUIRE(hi && lo && e && hs && ls && tsum && C == heads * 64 && Tp >= T, "quant_heads: bad arguments");
