@@ -142,7 +142,8 @@ int vela_quant_v(void* stream, const int32_t* X, int B, int Tk, int C, int heads
  * words (256 KiB per GPU, held until exit) instead of a caller buffer.  Requires B*heads*64 <= that maximum
  * (VELA_ERR_ARG otherwise).  The first call on a device looks up the array's device address; make it before any
  * stream capture.  All calls on a device share the array: calls that overlap on the GPU race, so order them on
- * one stream. */
+ * one stream.  The address stays cached for the life of the process: do not call it on a device after resetting
+ * that device (cudaDeviceReset). */
 #define VELA_QUANT_V_STATIC_MAX_COLS 65536
 int vela_quant_v_static(void* stream, const int32_t* X, int B, int Tk, int C, int heads, int Tkp, int8_t* vt_hi, int8_t* vt_lo, int32_t* ev, int64_t* vsum);
 
@@ -186,6 +187,10 @@ typedef void (*vela_tap_fn)(void* user, const char* name, const int32_t* data, s
 
 /* Load a POISD model file onto `device` (DevModel::load, src/engine.cu:11-70). NULL on failure. */
 vela_model* vela_model_load(int device, const char* path);
+/* The same from a POISD file image already in host memory (DevModel::load(int, const Poisd&), src/engine.h:18 --
+ * the reference's host parses the file once and hands the parsed model to every GPU).  The image is read during
+ * the call only.  NULL on failure. */
+vela_model* vela_model_load_memory(int device, const uint8_t* image, size_t bytes);
 void vela_model_free(vela_model* m);
 size_t vela_model_bytes(const vela_model* m);
 /* Engine(dm, cfg) (src/engine.cu:114-129). NULL on failure. */
@@ -213,6 +218,11 @@ int vela_engine_graph_kernels(const vela_engine* e);
  * makes vela_engine_collect / vela_engine_run return VELA_ERR_TIMEOUT).  Synchronises the engine's stream;
  * clear != 0 resets the word.  No reference counterpart (the reference's kernels have no bounded waits). */
 unsigned vela_engine_device_error(vela_engine* e, int clear);
+/* Self-check of the attention kernel (Engine::testAttention, src/engine.cu:575-597): seeded activations of random
+ * bit width 1..bits (0: zeros) for Q [B, Tq, 64 heads] and K, V [B, Tk, 64 heads], quantised by the library, then the
+ * tiled kernel against the exact definition written as plain GPU loops; returns the number of differing output
+ * words, or -1 on error.  No batches may be in flight. */
+long long vela_engine_test_attention(vela_engine* e, int B, int Tq, int Tk, int heads, int causal, int bits);
 int vela_engine_in_flight(const vela_engine* e);
 int vela_engine_batch(const vela_engine* e);
 size_t vela_engine_arena_peak(const vela_engine* e);

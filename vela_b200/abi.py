@@ -65,6 +65,7 @@ SIGNATURES = {
     "vela_fused_attention": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, P, P]),
     "vela_fused_attention_stalled": (I, [P] + [P] * 13 + [I] * 7 + [P, I, P, P, LL]),
     "vela_model_load": (P, [I, ctypes.c_char_p]),
+    "vela_model_load_memory": (P, [I, P, SZ]),
     "vela_model_free": (None, [P]),
     "vela_model_bytes": (SZ, [P]),
     "vela_engine_create": (P, [P, P]),
@@ -78,6 +79,7 @@ SIGNATURES = {
     "vela_engine_launch_device": (I, [P, P, P]),
     "vela_engine_graph_kernels": (I, [P]),
     "vela_engine_device_error": (U, [P, I]),
+    "vela_engine_test_attention": (LL, [P, I, I, I, I, I, I]),
     "vela_engine_in_flight": (I, [P]),
     "vela_engine_batch": (I, [P]),
     "vela_engine_arena_peak": (SZ, [P]),

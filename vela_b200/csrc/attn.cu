@@ -625,3 +625,58 @@ extern "C" int vela_fused_attention_stalled(void* stream, const int8_t* qhi, con
                         B, heads, Tq, Tqp, Tk, Tkp, causal != 0, lexp32, C, out, rowmax, o);
     });
 }
+
+namespace vela {
+namespace {
+// Exact attention written as plain loops, one thread per (head-batch g, query q): the definition restated
+// (src/kernels.cu:671-722) with 64-bit sums and no tiling, used only to check the tiled kernel (Engine::test_attention,
+// the reference's --test-attn).  Q, K: head-quantised planes [G, Tp, 64] + e; V^T planes [G, 64, Tkp] + ev.
+__global__ void attention_plain_kernel(const int8_t* __restrict__ qhi, const int8_t* __restrict__ qlo, const int32_t* __restrict__ eq, int Tqp,
+                                       const int8_t* __restrict__ khi, const int8_t* __restrict__ klo, const int32_t* __restrict__ ek,
+                                       const int8_t* __restrict__ vhi, const int8_t* __restrict__ vlo, const int32_t* __restrict__ ev,
+                                       int heads, int Tq, int Tk, int Tkp, int causal, const int32_t* __restrict__ L, int C, int32_t* __restrict__ out) {
+    const int g = blockIdx.y, q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= Tq) return;
+    const int nk = causal ? min(Tk, q + 1) : Tk;
+    auto qval = [&](int d) { const size_t i = (size_t(g) * Tqp + q) * 64 + d; return 256 * int(qhi[i]) + int(qlo[i]) + 128; };
+    auto score = [&](int k) {
+        i64 S = 0;
+        const size_t kb = (size_t(g) * Tkp + k) * 64;
+        for (int d = 0; d < 64; ++d) S += i64(qval(d)) * (256 * int(khi[kb + d]) + int(klo[kb + d]) + 128);
+        return int(rshr(S, 19 - eq[size_t(g) * Tqp + q] - ek[size_t(g) * Tkp + k]));
+    };
+    auto expl = [&](i64 z) -> i64 {
+        if (z >= (i64(1) << 20)) return 0;
+        const int i = int(z >> 10), f = int(z & 1023);
+        return int32_t(L[i] + (((i64(L[i + 1]) - L[i]) * f) >> 10));
+    };
+    int mx = INT_MIN;
+    for (int k = 0; k < nk; ++k) mx = max(mx, score(k));
+    i64 sum = 0;
+    for (int k = 0; k < nk; ++k) sum += expl(i64(mx) - score(k));
+    const i64 r = sum > 0 ? floor_div(i64(1) << 62, sum) : 0;
+    i64 O[64];
+    for (int d = 0; d < 64; ++d) O[d] = 0;
+    for (int k = 0; k < nk; ++k) {
+        const i64 E = expl(i64(mx) - score(k));
+        if (E <= 0) continue;
+        const i64 P = min(i64(32767), (E * r + (i64(1) << 46)) >> 47);
+        for (int d = 0; d < 64; ++d) {
+            const size_t vi = (size_t(g) * 64 + d) * Tkp + k;
+            O[d] += P * (256 * int(vhi[vi]) + int(vlo[vi]) + 128);
+        }
+    }
+    const int b = g / heads, h = g % heads;
+    for (int d = 0; d < 64; ++d) out[(size_t(b) * Tq + q) * C + h * 64 + d] = int(rshr(O[d], 15 - ev[g * 64 + d]));
+}
+}  // namespace
+
+void attention_plain(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, int Tqp, const int8_t* khi, const int8_t* klo,
+                     const int32_t* ek, const int8_t* vhi, const int8_t* vlo, const int32_t* ev, int B, int heads, int Tq, int Tk, int Tkp,
+                     bool causal, const int32_t* lexp, int C, int32_t* out) {
+    VELA_REQUIRE(B > 0 && heads > 0 && Tq > 0 && Tk > 0 && Tk <= Tkp && C == 64 * heads, "attention_plain: bad shape");
+    attention_plain_kernel<<<dim3(ceil_div(Tq, 64), B * heads), 64, 0, st>>>(qhi, qlo, eq, Tqp, khi, klo, ek, vhi, vlo, ev, heads, Tq, Tk, Tkp,
+                                                                             causal ? 1 : 0, lexp, C, out);
+    VELA_CUDA(cudaGetLastError());
+}
+}  // namespace vela

@@ -31,48 +31,61 @@ namespace vela {
 struct PoisdEntry { uint8_t dtype = 0; std::vector<uint32_t> dims; size_t off = 0, count = 0; };
 class Poisd {
 public:
+    // the file read into memory this object owns
     void load(const std::string& path) {
         FILE* f = std::fopen(path.c_str(), "rb");
         if (!f) throw Error(VELA_ERR_IO, "cannot open model " + path);
         std::fseek(f, 0, SEEK_END); const long sz = std::ftell(f); std::fseek(f, 0, SEEK_SET);
         if (sz < 12) { std::fclose(f); throw Error(VELA_ERR_IO, "model file too small"); }
-        data_.resize(size_t(sz));
-        const size_t got = std::fread(data_.data(), 1, data_.size(), f);
+        own_.resize(size_t(sz));
+        const size_t got = std::fread(own_.data(), 1, own_.size(), f);
         std::fclose(f);
-        if (got != data_.size()) throw Error(VELA_ERR_IO, "model read error");
+        if (got != own_.size()) throw Error(VELA_ERR_IO, "model read error");
+        parse(own_.data(), own_.size());
+    }
+    // a file image the caller keeps alive while this object is used (e.g. the bytes its host already read)
+    void view(const uint8_t* bytes, size_t n) {
+        if (!bytes || n < 12) throw Error(VELA_ERR_IO, "model image too small");
+        parse(bytes, n);
+    }
+    bool has(const std::string& n) const { return entries_.count(n) != 0; }
+    const PoisdEntry& get(const std::string& n) const {
+        auto it = entries_.find(n); if (it == entries_.end()) throw Error(VELA_ERR_IO, "model lacks tensor " + n); return it->second;
+    }
+    const int8_t* i8(const std::string& n) const { const auto& e = get(n); if (e.dtype != 0) throw Error(VELA_ERR_IO, n + " is not int8"); return reinterpret_cast<const int8_t*>(p_ + e.off); }
+    std::vector<int32_t> i32(const std::string& n) const {
+        const auto& e = get(n); if (e.dtype != 2) throw Error(VELA_ERR_IO, n + " is not int32");
+        std::vector<int32_t> v(e.count); std::memcpy(v.data(), p_ + e.off, e.count * 4); return v;
+    }
+    const std::map<std::string, PoisdEntry>& entries() const { return entries_; }
+private:
+    // container layout (src/poisd.cpp:17-33): "POISDv1\0", u32 count, then per tensor u16 name length, name, u8 dtype,
+    // u8 rank, u32 dims[rank], little-endian data
+    void parse(const uint8_t* p, size_t n) {
+        p_ = p; n_ = n; entries_.clear();
         static const uint8_t MAGIC[8] = {'P', 'O', 'I', 'S', 'D', 'v', '1', 0};
-        if (std::memcmp(data_.data(), MAGIC, 8) != 0) throw Error(VELA_ERR_IO, "bad magic (not a POISDv1 file)");
+        if (std::memcmp(p_, MAGIC, 8) != 0) throw Error(VELA_ERR_IO, "bad magic (not a POISDv1 file)");
         size_t pos = 8;
-        auto need = [&](size_t n) { if (pos + n > data_.size()) throw Error(VELA_ERR_IO, "truncated model file"); };
+        auto need = [&](size_t k) { if (pos + k > n_) throw Error(VELA_ERR_IO, "truncated model file"); };
         need(4); const uint32_t count = rd32(pos); pos += 4;
         static const size_t SZ[4] = {1, 2, 4, 1};
         for (uint32_t i = 0; i < count; ++i) {
-            need(2); const uint16_t nl = uint16_t(data_[pos] | (data_[pos + 1] << 8)); pos += 2;
-            need(size_t(nl) + 2); std::string name(reinterpret_cast<const char*>(&data_[pos]), nl); pos += nl;
-            PoisdEntry e; e.dtype = data_[pos]; const uint8_t nd = data_[pos + 1]; pos += 2;
+            need(2); const uint16_t nl = uint16_t(p_[pos] | (p_[pos + 1] << 8)); pos += 2;
+            need(size_t(nl) + 2); std::string name(reinterpret_cast<const char*>(p_ + pos), nl); pos += nl;
+            PoisdEntry e; e.dtype = p_[pos]; const uint8_t nd = p_[pos + 1]; pos += 2;
             if (e.dtype > 3) throw Error(VELA_ERR_IO, "bad dtype in " + name);
             need(size_t(4) * nd); e.count = 1;
             for (int d = 0; d < nd; ++d) { e.dims.push_back(rd32(pos)); e.count *= e.dims.back(); pos += 4; }
             need(e.count * SZ[e.dtype]); e.off = pos; pos += e.count * SZ[e.dtype];
             entries_.emplace(std::move(name), std::move(e));
         }
-        if (pos != data_.size()) throw Error(VELA_ERR_IO, "trailing data in model file");
-        for (const char* n : {"unet.conv_in.w", "unet.conv_out.w", "te.tok.w", "te.pos", "lut.gauss", "lut.exp", "lut.sigmoid", "lut.phi", "c.sig", "c.cin"})
-            if (!has(n)) throw Error(VELA_ERR_IO, std::string("model lacks tensor ") + n);
+        if (pos != n_) throw Error(VELA_ERR_IO, "trailing data in model file");
+        for (const char* t : {"unet.conv_in.w", "unet.conv_out.w", "te.tok.w", "te.pos", "lut.gauss", "lut.exp", "lut.sigmoid", "lut.phi", "c.sig", "c.cin"})
+            if (!has(t)) throw Error(VELA_ERR_IO, std::string("model lacks tensor ") + t);
     }
-    bool has(const std::string& n) const { return entries_.count(n) != 0; }
-    const PoisdEntry& get(const std::string& n) const {
-        auto it = entries_.find(n); if (it == entries_.end()) throw Error(VELA_ERR_IO, "model lacks tensor " + n); return it->second;
-    }
-    const int8_t* i8(const std::string& n) const { const auto& e = get(n); if (e.dtype != 0) throw Error(VELA_ERR_IO, n + " is not int8"); return reinterpret_cast<const int8_t*>(&data_[e.off]); }
-    std::vector<int32_t> i32(const std::string& n) const {
-        const auto& e = get(n); if (e.dtype != 2) throw Error(VELA_ERR_IO, n + " is not int32");
-        std::vector<int32_t> v(e.count); std::memcpy(v.data(), &data_[e.off], e.count * 4); return v;
-    }
-    const std::map<std::string, PoisdEntry>& entries() const { return entries_; }
-private:
-    uint32_t rd32(size_t p) const { return uint32_t(data_[p]) | (uint32_t(data_[p + 1]) << 8) | (uint32_t(data_[p + 2]) << 16) | (uint32_t(data_[p + 3]) << 24); }
-    std::vector<uint8_t> data_;
+    uint32_t rd32(size_t q) const { return uint32_t(p_[q]) | (uint32_t(p_[q + 1]) << 8) | (uint32_t(p_[q + 2]) << 16) | (uint32_t(p_[q + 3]) << 24); }
+    std::vector<uint8_t> own_;
+    const uint8_t* p_ = nullptr; size_t n_ = 0;
     std::map<std::string, PoisdEntry> entries_;
 };
 
@@ -191,10 +204,10 @@ public:
     const Norm& norm(const std::string& n) const { auto it = norms.find(n); if (it == norms.end()) throw Error(VELA_ERR_IO, "model lacks norm " + n); return it->second; }
     bool has_lin(const std::string& n) const { return lins.count(n) != 0; }
 
-    void load(int dev, const std::string& path) {
+    void load(int dev, const std::string& path) { Poisd f; f.load(path); load(dev, f); }
+    void load(int dev, const Poisd& f) {
         device = dev;
         VELA_CUDA(cudaSetDevice(dev));
-        Poisd f; f.load(path);
         std::map<std::string, HostLin> hl;
         // every linear the file holds: <base>.w int8 [N, K] with per-channel <base>.m / .s / .b
         const std::set<std::string> k3 = kernel3x3_names();
@@ -451,6 +464,50 @@ public:
         VELA_CUDA(cudaMemcpyAsync(dx0, dOut_[0], size_t(32768) * B_, cudaMemcpyDeviceToDevice, st_));
     }
     int graph_kernels() const { return graph_kernels_; }
+    // Self-check of the attention kernel (Engine::testAttention, src/engine.cu:575-597): seeded activations of random
+    // bit width 1..bits (0: all zero) for Q [B, Tq, C] and K, V [B, Tk, C], quantised by the library's quantisers, then
+    // the tiled kernel against the plain-loop exact definition; returns the number of differing output words.
+    long test_attention(int B, int Tq, int Tk, int heads, bool causal, int bits) {
+        VELA_REQUIRE(inflight_ == 0, "test_attention: batches in flight");
+        VELA_REQUIRE(B > 0 && Tq > 0 && Tk > 0 && Tk <= 4096 && heads > 0 && bits >= 0 && bits <= 31, "test_attention: bad arguments");
+        VELA_CUDA(cudaSetDevice(m_.device));
+        const int C = 64 * heads, G = B * heads, Tqp = int(align_up(Tq, 128)), Tkp = int(align_up(Tk, 64));
+        const size_t mark = arena_.off;
+        uint64_t state = 0x243F6A8885A308D3ull ^ (uint64_t(B) << 48) ^ (uint64_t(Tq) << 24) ^ uint64_t(Tk);
+        auto draw = [&](int T) {
+            std::vector<int32_t> h(size_t(B) * T * C);
+            for (auto& v : h) {
+                state += 0x9E3779B97F4A7C15ull;
+                uint64_t z = (state ^ (state >> 30)) * 0xBF58476D1CE4E5B9ull; z = (z ^ (z >> 27)) * 0x94D049BB133111EBull; z ^= z >> 31;
+                const int w = bits ? 1 + int((z >> 40) % uint64_t(bits)) : 0;
+                v = w ? int32_t(int64_t(z & ((uint64_t(1) << w) - 1)) - (int64_t(1) << (w - 1))) : 0;
+            }
+            int32_t* d = static_cast<int32_t*>(arena_.alloc(h.size() * 4));
+            VELA_CUDA(cudaMemcpyAsync(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice, st_));
+            VELA_CUDA(cudaStreamSynchronize(st_));
+            return d;
+        };
+        const int32_t *xq = draw(Tq), *xk = draw(Tk), *xv = draw(Tk);
+        HeadQ q = head_alloc(B, heads, Tq, Tqp), k = head_alloc(B, heads, Tk, Tkp);
+        quant_heads(st_, xq, B, Tq, C, heads, Tqp, q.hi, q.lo, q.e, q.hs, q.ls, q.ts, 0);
+        quant_heads(st_, xk, B, Tk, C, heads, Tkp, k.hi, k.lo, k.e, k.hs, k.ls, k.ts, 0);
+        Tensor v; v.B = B; v.T = Tk; v.C = C; v.d = const_cast<int32_t*>(xv);
+        const KV kv = kv_of(k, v, heads);
+        int32_t* got = static_cast<int32_t*>(arena_.alloc(size_t(B) * Tq * C * 4));
+        int32_t* ref = static_cast<int32_t*>(arena_.alloc(size_t(B) * Tq * C * 4));
+        fused_attention(st_, q.hi, q.lo, q.e, q.hs, q.ls, kv.khi, kv.klo, kv.ek, kv.ksum, kv.vhi, kv.vlo, kv.ev, kv.vsum,
+                        B, heads, Tq, Tqp, Tk, Tkp, causal, m_.lut_exp, C, got, nullptr, lo_);
+        attention_plain(st_, q.hi, q.lo, q.e, Tqp, kv.khi, kv.klo, kv.ek, kv.vhi, kv.vlo, kv.ev, B, heads, Tq, Tk, Tkp, causal, m_.lut_exp, C, ref);
+        std::vector<int32_t> hg(size_t(B) * Tq * C), hr(hg.size());
+        VELA_CUDA(cudaMemcpyAsync(hg.data(), got, hg.size() * 4, cudaMemcpyDeviceToHost, st_));
+        VELA_CUDA(cudaMemcpyAsync(hr.data(), ref, hr.size() * 4, cudaMemcpyDeviceToHost, st_));
+        VELA_CUDA(cudaStreamSynchronize(st_));
+        arena_.off = mark;
+        if (const unsigned v2 = device_error(true)) throw Error(VELA_ERR_TIMEOUT, "test_attention: a bounded wait gave up (device error code " + std::to_string(v2) + ")");
+        long bad = 0;
+        for (size_t i = 0; i < hg.size(); ++i) bad += hg[i] != hr[i];
+        return bad;
+    }
     // the engine's device error word (synchronises the engine's stream); clear: reset it to zero
     unsigned device_error(bool clear) {
         VELA_CUDA(cudaSetDevice(m_.device));
@@ -863,6 +920,16 @@ extern "C" vela_model* vela_model_load(int device, const char* path) {
     });
     return rc == VELA_OK ? out : nullptr;
 }
+extern "C" vela_model* vela_model_load_memory(int device, const uint8_t* image, size_t bytes) {
+    vela_model* out = nullptr;
+    const int rc = guarded("vela_model_load_memory", [&] {
+        Poisd f; f.view(image, bytes);
+        std::unique_ptr<vela_model> m(new vela_model());
+        m->m.load(device, f);
+        out = m.release();
+    });
+    return rc == VELA_OK ? out : nullptr;
+}
 extern "C" void vela_model_free(vela_model* m) { delete m; }
 extern "C" size_t vela_model_bytes(const vela_model* m) { return m ? m->m.bytes : 0; }
 extern "C" vela_engine* vela_engine_create(const vela_model* m, const vela_engine_config* cfg) {
@@ -899,6 +966,14 @@ extern "C" int vela_engine_graph_kernels(const vela_engine* e) { return e ? e->e
 extern "C" unsigned vela_engine_device_error(vela_engine* e, int clear) {
     if (!e) return 0;
     try { return e->e->device_error(clear != 0); } catch (...) { return 0xFFFFFFFFu; }
+}
+extern "C" long long vela_engine_test_attention(vela_engine* e, int B, int Tq, int Tk, int heads, int causal, int bits) {
+    long long bad = -1;
+    const int rc = guarded("vela_engine_test_attention", [&] {
+        VELA_REQUIRE(e, "null engine");
+        bad = e->e->test_attention(B, Tq, Tk, heads, causal != 0, bits);
+    });
+    return rc == VELA_OK ? bad : -1;
 }
 extern "C" int vela_engine_in_flight(const vela_engine* e) { return e ? e->e->in_flight() : 0; }
 extern "C" int vela_engine_batch(const vela_engine* e) { return e ? e->e->batch() : 0; }

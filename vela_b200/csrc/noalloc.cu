@@ -13,7 +13,9 @@
 // cudaGetSymbolAddress while that device is current, and later calls reuse it.  Every call on a device shares
 // the same array and it keeps the last call's contents, so each call clears the G*64 words it uses before the
 // column-max kernel runs, and two calls whose work overlaps on the GPU (different streams, or different host
-// threads on one device) race on it: such callers must order their calls on one stream.
+// threads on one device) race on it: such callers must order their calls on one stream.  The resolved address
+// belongs to the device's primary context as it was at the first call: a process that resets a device
+// (cudaDeviceReset) must not call this entry point on that device again.
 #include "ops.h"
 #include "status.h"
 #include "host_util.h"

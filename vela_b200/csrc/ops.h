@@ -37,4 +37,8 @@ void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, cons
                      const int8_t* vthi, const int8_t* vtlo, const int32_t* ev, const i64* vsum,
                      int B, int heads, int Tq, int Tqp, int Tk, int Tkp, bool causal, const int32_t* lexp, int C, int32_t* out, uint32_t* rowmax,
                      const LaunchOpts& o = LaunchOpts());
+// the exact definition as plain loops on the GPU (one thread per query), for checking fused_attention
+void attention_plain(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, const int32_t* eq, int Tqp, const int8_t* khi, const int8_t* klo,
+                     const int32_t* ek, const int8_t* vhi, const int8_t* vlo, const int32_t* ev, int B, int heads, int Tq, int Tk, int Tkp,
+                     bool causal, const int32_t* lexp, int C, int32_t* out);
 }  // namespace vela
