@@ -11,7 +11,7 @@ kernel computes and checks it against the spec form on edge values and seeded ra
 - lut_act_s: x * lut / 2^16 rounded needs no saturation when 0 <= lut <= 65536;
 - norm_val (rowops.cu): the binary64 quotient formed with the 1.5 * 2^52 constant and one fma residual test
   ==  floor((d 2^(25-e) + sd) / (2 sd));
-- the attention softmax forms (attn.cu): the 32-bit score (hh M + mul.hi(T, 2^(32-a))) >> b, its mixed-exponent
+- the attention softmax forms (attn.cu): the 32-bit score (hh M + (T >> a)) >> b, its mixed-exponent
   variant, the exp table interpolated with one mad.hi, and P from the reciprocal's 32-bit halves;
 - the int32 staging quantiser is covered by the GPU parity tests.
 """
@@ -186,11 +186,9 @@ def mulhi32(a, b):          # mul.hi.s32 of two int32 values
 
 
 def div_pow2_model(hh, T, sh):
-    """attn.cu div_pow2 then >> b, for a = min(sh, 16), b = sh - a, M = 2^(16-a), A = 2^(32-a):
-    (hh M + mul.hi(T, A)) mod 2^32, then >> b"""
+    """attn.cu div_pow2 then >> b, for a = min(sh, 16), b = sh - a, M = 2^(16-a): (hh M + (T >> a)) mod 2^32, then >> b"""
     a = min(sh, 16)
-    assert 0 < (1 << (32 - a)) < 2**31
-    return s32(hh * (1 << (16 - a)) + mulhi32(T, 1 << (32 - a))) >> (sh - a)
+    return s32(hh * (1 << (16 - a)) + (T >> a)) >> (sh - a)
 
 
 def _score_operands(rnd, n):
@@ -213,7 +211,7 @@ def _score_operands(rnd, n):
 
 
 def test_attention_score_32bit_form():
-    """one key exponent per chunk: (hh M + mul.hi(T, 2^(32-a))) >> b == rshr(S, sh) for every shift the fast path takes"""
+    """one key exponent per chunk: (hh M + (T >> a)) >> b == rshr(S, sh) for every shift the fast path takes"""
     rnd = random.Random(21)
     ops = _score_operands(rnd, 300)
     ops.append((64 * 128 * 128, 0, 0, 0, 0, 64 * 128 * 128 * 65536))      # every plane product at its largest magnitude
@@ -237,7 +235,7 @@ def test_attention_score_mixed_exponents():
                 b0 = shq - emax - a0
                 for ek in range(0, emax + 1):
                     T = 256 * xx + ll + kc + cq + ((1 << (shq - 1)) >> ek)
-                    got = s32(hh * (1 << (16 - a0)) + mulhi32(T, 1 << (32 - a0))) >> (b0 + emax - ek)
+                    got = s32(hh * (1 << (16 - a0)) + (T >> a0)) >> (b0 + emax - ek)
                     assert got == rshr(S, shq - ek), (shq, emax, ek)
 
 

@@ -92,13 +92,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // of the SM sub-partition (each issues a warp instruction every other cycle): multiplies, multiply-highs (right shifts
 // by a power of two) and multiply-adds run on the FMA pipe, adds / min / max / logic / funnel shifts on the ALU pipe.
 // The multipliers that are powers of two come from kernel arguments (OpK), so the compiler keeps the multiply forms.
+// Measured on B200: mad.lo, shifts, prmt, min and adds issue at half the warp rate; mad.hi / mul.hi at a quarter, so
+// right shifts stay shifts.
 __device__ __forceinline__ int mad_lo(int a, int b, int c) { int d; asm("mad.lo.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
 __device__ __forceinline__ int mul_lo(int a, int b) { int d; asm("mul.lo.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d; }
 __device__ __forceinline__ int mad_hi(int a, int b, int c) { int d; asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
-__device__ __forceinline__ int mul_hi(int a, int b) { int d; asm("mul.hi.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d; }
 __device__ __forceinline__ uint32_t mad_hi_u(uint32_t a, uint32_t b, uint32_t c) { uint32_t d; asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
 __device__ __forceinline__ uint32_t mad_lo_u(uint32_t a, uint32_t b, uint32_t c) { uint32_t d; asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d; }
-__device__ __forceinline__ uint64_t mad_wide_u(uint32_t a, uint32_t b, uint64_t c) { uint64_t d; asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c)); return d; }
 __device__ __forceinline__ int2 lds_v2(uint32_t addr) { int2 v; asm("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr)); return v; }
 
 // ---- score arithmetic (fast forms; every shift sh = 19 - eq - ek of the chunk lies in [5, 19])
@@ -106,17 +106,16 @@ __device__ __forceinline__ int2 lds_v2(uint32_t addr) { int2 v; asm("ld.shared.v
 // is computed in 32 bits as  s = (hh M + (T >> a)) >> b  with a = min(sh, 16), b = sh - a, M = 2^(16 - a):
 //   sh <= 16: 65536 hh = 2^sh (hh M), so the quotient is hh M + floor(T / 2^sh);
 //   sh > 16:  floor(floor((65536 hh + T) / 2^16) / 2^b) = (hh + (T >> 16)) >> b.
-// |s| < 2^31 (|S| < 2^36, sh >= 5), so hh M + (T >> a) is formed modulo 2^32: an intermediate wrap cancels.  T >> a is
-// the multiply-high of T by 2^(32 - a) (a >= 5, so the multiplier is a positive int32).
+// |s| < 2^31 (|S| < 2^36, sh >= 5), so hh M + (T >> a) is formed modulo 2^32: an intermediate wrap cancels.
 // A chunk whose keys have different exponents takes the smallest shift sh0 = 19 - eq - max ek for the division
 // and shifts each key's result right by the remainder d = max ek - ek (nested floors), with each key's own rounding
 // term 2^(19 - eq - ek - 1) in T.
-struct ShiftSplit { int a, b; int M, A; };
+struct ShiftSplit { int a, b; int M; };
 __device__ __forceinline__ ShiftSplit split_shift(int sh) {
     const int a = min(sh, 16);
-    return ShiftSplit{a, sh - a, 1 << (16 - a), 1 << (32 - a)};
+    return ShiftSplit{a, sh - a, 1 << (16 - a)};
 }
-__device__ __forceinline__ int div_pow2(int hh, int T, const ShiftSplit& p) { return mad_lo(hh, p.M, mul_hi(T, p.A)); }
+__device__ __forceinline__ int div_pow2(int hh, int T, const ShiftSplit& p) { return mad_lo(hh, p.M, T >> p.a); }
 
 // ---- exp table: E = L[i] + floor((L[i+1] - L[i]) f / 2^10) for z = mx - s, i = min(z, 2^20) >> 10, f = its low 10 bits
 // (index 1024 is a sentinel (0, 0): E = 0 from z = 2^20 on).  Fast table (every L[i] in [0, 2^31) and every difference
@@ -242,12 +241,12 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
         }
     } else if constexpr (PASS == 1) {
         if constexpr (TF) {
-            // each E < 2^31: a pair fits 32 bits, added to the 64-bit sum by one wide multiply-add
+            // each E < 2^31: a pair fits 32 bits (added on the FMA pipe), then to the 64-bit sum on the ALU pipe
             #pragma unroll
             for (int u = 0; u < 16; u += 2) {
                 int e0 = exp_fast(zclamp(mx, s[u]), lut_addr, k), e1 = exp_fast(zclamp(mx, s[u + 1]), lut_addr, k);
                 if (!FULL) { e0 = (vmask >> u) & 1u ? e0 : 0; e1 = (vmask >> (u + 1)) & 1u ? e1 : 0; }
-                sum = mad_wide_u(uint32_t(mad_lo(e0, k.c1, e1)), uint32_t(k.c1), sum);
+                sum += uint32_t(mad_lo(e0, k.c1, e1));
             }
         } else {
             #pragma unroll
