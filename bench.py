@@ -67,13 +67,15 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu", "norms"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu", "qkv", "norms"], default=None,
                     help="run only the named kernel(s) at the BASELINE config shape (attention: config 2, gemm: config 1, "
                          "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 for 640 ch 32x32 / 1280 ch 16x16), "
                          "linear: the UNet's int32-input linear with residual at 64x64 (M 32768, K --linear-k, N 320), "
-                         "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); norms: GroupNorm statistics, "
+                         "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); qkv: the merged q|k|v GEMM with head "
+                         "quantisation (M 32768, K 320, N 960); norms: GroupNorm statistics, "
                          "GroupNorm+SiLU apply and LayerNorm->planes at 320 ch 64x64, each timed alone; "
-                         "print their CUDA-event times as one JSON line and exit")
+                         "print their CUDA-event times as one JSON line and exit; with --impl reference the reference's own "
+                         "kernels at the same shapes")
     ap.add_argument("--linear-k", type=int, default=320)
     ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2])
     a = ap.parse_args()
@@ -421,7 +423,7 @@ class LinearCase:
         from vela_b200 import abi
         self.t, self.V, self.L = torch, V, V.lib()
         M = 32768
-        N = 2560 if kind == "geglu" else 320
+        N = {"geglu": 2560, "qkv": 960}.get(kind, 320)
         g = torch.Generator(device=device); g.manual_seed(4)
         ri = lambda lo, hi, shape: torch.randint(lo, hi, shape, generator=g, device=device, dtype=torch.int32)
         self.W = ri(-127, 128, (N, K)).to(torch.int8)
@@ -430,7 +432,20 @@ class LinearCase:
         self.cst = cst
         self.rm_out = torch.zeros((M,), dtype=torch.int32, device=device)
         a = abi.ASrc(); E = abi.AEpi()
-        if kind == "geglu":
+        if kind == "qkv":
+            q = ri(-32768, 32768, (M, K))
+            self.hi = (q >> 8).to(torch.int8); self.lo = ((q & 255) - 128).to(torch.int8); self.e = ri(0, 6, (M,))
+            a.src = abi.SRC_I8; a.hi = self.hi.data_ptr(); a.lo = self.lo.data_ptr(); a.ld8 = K; a.e = self.e.data_ptr()
+            heads, T, C = 5, 4096, 320
+            G = (M // T) * heads
+            z = lambda *s_, dt: torch.zeros(s_, dtype=dt, device=device)
+            self.qb = [z(G, T, 64, dt=torch.int8), z(G, T, 64, dt=torch.int8), z(G, T, dt=torch.int32)] + [z(G, T, dt=torch.int64) for _ in range(3)]
+            self.kb = [z(G, T, 64, dt=torch.int8), z(G, T, 64, dt=torch.int8), z(G, T, dt=torch.int32)] + [z(G, T, dt=torch.int64) for _ in range(3)]
+            self.Y = z(M, C, dt=torch.int32)
+            E.epi = abi.EPI_QKV; E.Y2 = self.Y.data_ptr(); E.heads = heads; E.T = T; E.TpQ = T; E.TpK = T; E.C = C
+            E.qhi, E.qlo, E.qe, E.qhs, E.qls, E.qts = [x.data_ptr() for x in self.qb]
+            E.khi, E.klo, E.ke, E.khs, E.kls, E.kts = [x.data_ptr() for x in self.kb]
+        elif kind == "geglu":
             q = ri(-32768, 32768, (M, K))
             self.hi = (q >> 8).to(torch.int8); self.lo = ((q & 255) - 128).to(torch.int8); self.e = ri(0, 6, (M,))
             a.src = abi.SRC_I8; a.hi = self.hi.data_ptr(); a.lo = self.lo.data_ptr(); a.ld8 = K; a.e = self.e.data_ptr()
@@ -477,6 +492,185 @@ class LinearCase:
             rep["planar_quant_ms"] = round(_time_ms(self.stream, quant), 4)
             rep["planar_gemm_ms"] = round(_time_ms(self.stream, gemm), 4)
         return rep
+
+
+# ------------------------------------------------------------------ the reference's kernels at the config shapes
+class RefKernels:
+    """The reference's own kernels (oracle/_ref/libvela_ref.so: src/kernels.cu, gemm_hl.cu, attn.cu, gemm.cu compiled
+    from its sources) timed with CUDA events at the same shapes and value distributions as our --kernel cases.
+    Inputs are quantised by the reference's own quantisers, so this process loads no library of the product."""
+
+    def __init__(self, device):
+        import ctypes
+        import torch
+        so = os.path.join(ROOT, "oracle", "_ref", "libvela_ref.so")
+        if not os.path.exists(so):
+            raise FileNotFoundError(so)
+        self.L = ctypes.CDLL(so)
+        self.L.ref_last_error.restype = ctypes.c_char_p
+        self.L.ref_set_sync.argtypes = [ctypes.c_int]
+        self.t, self.dev, self.c = torch, device, ctypes
+        self.L.ref_set_sync(0)
+
+    def P(self, x):
+        return self.c.c_void_p(x.data_ptr()) if x is not None else None
+
+    def ok(self, rc):
+        if rc != 0:
+            raise RuntimeError("reference kernel: " + self.L.ref_last_error().decode())
+
+    def time(self, fn, warmup=3, iters=10):
+        torch = self.t
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s = torch.cuda.default_stream(self.dev)        # the harness launches on the legacy default stream
+        e0.record(s)
+        for _ in range(iters):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    def ri(self, g, lo, hi, shape, dt=None):
+        x = self.t.randint(lo, hi, shape, generator=g, device=self.dev, dtype=self.t.int32)
+        return x if dt is None else x.to(dt)
+
+    def cst(self, g, W):
+        N = W.shape[0]
+        c = self.t.zeros((N, 4), dtype=self.t.int32, device=self.dev)
+        c[:, 0] = self.ri(g, 16384, 32768, (N,)); c[:, 1] = self.ri(g, 20, 30, (N,)); c[:, 2] = self.ri(g, -50000, 50000, (N,))
+        c[:, 3] = W.to(self.t.int32).sum(1)
+        return c
+
+    def attention(self):
+        """config 2: 8 x 5 heads x 4096 x 4096 x 64 on int16-range activations, the reference's k_fused_attention"""
+        torch, P, L = self.t, self.P, self.L
+        B, heads, T = ATTN_SHAPE["B"], ATTN_SHAPE["heads"], ATTN_SHAPE["T"]
+        C, G, Tp = 64 * heads, B * heads, (T + 127) // 128 * 128
+        g = torch.Generator(device=self.dev); g.manual_seed(2)
+        X = [self.ri(g, -32768, 32768, (B, T, C)) for _ in range(3)]
+        z = lambda *s, dt: torch.zeros(s, dtype=dt, device=self.dev)
+        q = [z(G, Tp, 64, dt=torch.int8), z(G, Tp, 64, dt=torch.int8), z(G, Tp, dt=torch.int32)] + [z(G, Tp, dt=torch.int64) for _ in range(3)]
+        k = [z(G, Tp, 64, dt=torch.int8), z(G, Tp, 64, dt=torch.int8), z(G, Tp, dt=torch.int32)] + [z(G, Tp, dt=torch.int64) for _ in range(3)]
+        v = [z(G, 64, Tp, dt=torch.int8), z(G, 64, Tp, dt=torch.int8), z(G, 64, dt=torch.int32), z(G, 64, dt=torch.int64)]
+        self.L.ref_set_sync(1)
+        self.ok(L.ref_quant_heads(P(X[0]), B, T, C, heads, Tp, *[P(x) for x in q]))
+        self.ok(L.ref_quant_heads(P(X[1]), B, T, C, heads, Tp, *[P(x) for x in k]))
+        self.ok(L.ref_quant_v(P(X[2]), B, T, C, heads, Tp, *[P(x) for x in v], P(z(G, 64, dt=torch.int32))))
+        self.L.ref_set_sync(0)
+        lexp = torch.from_numpy(np.rint(1073741824.0 * np.exp(-np.arange(1025) / 64.0)).astype(np.int64)).to(self.dev)
+        gmx, gr = z(G * Tp, dt=torch.int32), z(G * Tp, dt=torch.int64)
+        out, rm = z(B, T, C, dt=torch.int32), z(B * T, dt=torch.int32)
+        run = lambda: self.ok(L.ref_fused_attention(P(q[0]), P(q[1]), P(q[2]), P(q[3]), P(q[4]), P(k[0]), P(k[1]), P(k[2]), P(k[5]),
+                                                    P(v[0]), P(v[1]), P(v[2]), P(v[3]), B, heads, T, Tp, T, Tp, 0, P(lexp), C,
+                                                    P(gmx), P(gr), P(out), P(rm)))
+        return {"kernel": "reference k_fused_attention (config 2)", "ms": round(self.time(run), 4)}
+
+    def gemm(self):
+        """config 1: planar A 4096 x 320 (int16 range), W 320 x 320, the reference's gemm_hl (k_gemm_hl2)"""
+        torch, P, L = self.t, self.P, self.L
+        M, N, K = 4096, 320, 320
+        g = torch.Generator(device=self.dev); g.manual_seed(1)
+        q = self.ri(g, -32768, 32768, (M, K))
+        hi, lo = (q >> 8).to(torch.int8), ((q & 255) - 128).to(torch.int8)
+        W = self.ri(g, -127, 128, (N, K), torch.int8); cst = self.cst(g, W); e = self.ri(g, 0, 12, (M,))
+        Y = torch.empty((M, N), dtype=torch.int32, device=self.dev)
+        run = lambda: self.ok(L.ref_gemm_hl(P(hi), P(lo), K, M, M, P(W), K, N, N, K, P(cst), P(e), P(Y), N, None, 0, 0, None, None, None, None))
+        ms = self.time(run)
+        return {"kernel": "reference gemm_hl planar (config 1)", "M": M, "N": N, "K": K, "ms": round(ms, 4), "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
+
+    def gn_conv(self, level):
+        """config 3: GroupNorm + SiLU of int16-range NHWC [8, H*W, C], then the 3x3 conv C -> C the way the reference's
+        engine runs it at these depths (9C > 1536: pixel max, im2col, cuBLASLt, epilogue; src/engine.cu:254-280), and its
+        fused-loader gemm_hl (SRC_CONV32) for comparison"""
+        torch, P, L = self.t, self.P, self.L
+        Hh, C = GnConvCase.LEVELS[level]
+        B, T, N, K = 8, Hh * Hh, C, 9 * C
+        g = torch.Generator(device=self.dev); g.manual_seed(3)
+        X = self.ri(g, -32768, 32768, (B, T, C))
+        gam, beta = self.ri(g, 65536 - 16384, 65536 + 16384, (C,)), self.ri(g, -8192, 8192, (C,))
+        xs = np.arange(2049, dtype=np.float64) / 64.0 - 16.0
+        Lsig = torch.from_numpy(np.rint(65536.0 / (1.0 + np.exp(-xs))).astype(np.int32)).to(self.dev)
+        gs = torch.zeros((B * 32, 6), dtype=torch.int64, device=self.dev)
+        Y, pm = torch.empty((B, T, C), dtype=torch.int32, device=self.dev), torch.empty((B * T,), dtype=torch.int32, device=self.dev)
+        W = self.ri(g, -127, 128, (N, K), torch.int8); cst = self.cst(g, W)
+        e = torch.empty((B * T,), dtype=torch.int32, device=self.dev)
+        planes = torch.empty((2 * B * T, K), dtype=torch.int8, device=self.dev)
+        Cs = torch.empty((2 * B * T, N), dtype=torch.int32, device=self.dev)
+        out = torch.empty((B * T, N), dtype=torch.int32, device=self.dev)
+        def gn():
+            self.ok(L.ref_gn_stats(P(X), B, T, C, 32, 100000, P(gs)))
+            self.ok(L.ref_gn_apply_row(P(X), B, T, C, 32, P(gs), P(gam), P(beta), P(Lsig), P(Y), P(pm), None, None, None, 0))
+        def conv_lt():
+            self.ok(L.ref_pixmax(P(Y), B * T, C, P(pm)))
+            self.ok(L.ref_im2col3(P(Y), P(pm), B, Hh, Hh, C, 1, P(planes), self.c.c_void_p(planes.data_ptr() + B * T * K), P(e), K))
+            self.ok(L.ref_gemm_lt(P(planes), B * T, B * T, P(W), N, N, K, P(cst), P(e), P(Cs), P(out), N, None))
+        def conv_hl():
+            self.ok(L.ref_gemm_conv(P(Y), B, Hh, Hh, C, 1, P(pm), P(e), B * T, P(W), K, N, N, K, P(cst), P(out), N, None))
+        gn()
+        gms, lms, hms = self.time(gn), self.time(conv_lt), self.time(conv_hl)
+        ops = 2 * 2 * B * T * N * K
+        return {"kernel": "reference GroupNorm+SiLU -> 3x3 conv (config 3)", "B": B, "HW": Hh, "C": C, "gn_ms": round(gms, 4),
+                "conv_engine_path_ms": round(lms, 4), "conv_engine_path_int8_tops": round(ops / lms / 1e9, 2),
+                "conv_fused_loader_ms": round(hms, 4), "conv_fused_loader_int8_tops": round(ops / hms / 1e9, 2)}
+
+    def norms(self):
+        """GroupNorm statistics, GroupNorm + SiLU apply and LayerNorm -> planes at 320 ch 64x64, each timed alone"""
+        torch, P, L = self.t, self.P, self.L
+        B, T, C = 8, 4096, 320
+        g = torch.Generator(device=self.dev); g.manual_seed(3)
+        X = self.ri(g, -32768, 32768, (B, T, C))
+        gam, beta = self.ri(g, 65536 - 16384, 65536 + 16384, (C,)), self.ri(g, -8192, 8192, (C,))
+        xs = np.arange(2049, dtype=np.float64) / 64.0 - 16.0
+        Lsig = torch.from_numpy(np.rint(65536.0 / (1.0 + np.exp(-xs))).astype(np.int32)).to(self.dev)
+        gs = torch.zeros((B * 32, 6), dtype=torch.int64, device=self.dev)
+        Y, pm = torch.empty((B, T, C), dtype=torch.int32, device=self.dev), torch.empty((B * T,), dtype=torch.int32, device=self.dev)
+        hi, lo = torch.empty((B * T, C), dtype=torch.int8, device=self.dev), torch.empty((B * T, C), dtype=torch.int8, device=self.dev)
+        e = torch.empty((B * T,), dtype=torch.int32, device=self.dev)
+        stats = lambda: self.ok(L.ref_gn_stats(P(X), B, T, C, 32, 100000, P(gs)))
+        apply = lambda: self.ok(L.ref_gn_apply_row(P(X), B, T, C, 32, P(gs), P(gam), P(beta), P(Lsig), P(Y), P(pm), None, None, None, 0))
+        ln = lambda: self.ok(L.ref_lnorm_q(P(X), B * T, C, P(gam), P(beta), 100000, P(hi), P(lo), P(e), C))
+        stats()
+        ts, ta, tl = self.time(stats), self.time(apply), self.time(ln)
+        nb = B * T * C * 4
+        return {"kernel": "reference norms (320 ch 64x64)", "gn_stats_ms": round(ts, 4), "gn_stats_gbs": round(2 * nb / ts / 1e6, 1),
+                "gn_apply_ms": round(ta, 4), "gn_apply_gbs": round((2 * nb + B * T * 4) / ta / 1e6, 1),
+                "lnorm_q_ms": round(tl, 4), "lnorm_q_gbs": round((nb + nb // 2) / tl / 1e6, 1)}
+
+    def linear(self, kind, K):
+        """the UNet's 64x64-level linears: int32 input quantised on load (K 320 / 1280, N 320, + residual + row max), the GEGLU
+        GEMM (K 320, N 2560), the merged q|k|v GEMM with head quantisation (K 320, N 960); the reference's gemm_hl forms"""
+        torch, P, L = self.t, self.P, self.L
+        M = 32768
+        N = {"geglu": 2560, "qkv": 960}.get(kind, 320)
+        g = torch.Generator(device=self.dev); g.manual_seed(4)
+        W = self.ri(g, -127, 128, (N, K), torch.int8); cst = self.cst(g, W)
+        if kind == "linear":
+            X = self.ri(g, -(1 << 20), 1 << 20, (M, K)); rm = X.abs().amax(1).to(torch.int32)
+            R = self.ri(g, -(1 << 20), 1 << 20, (M, N)); Y = torch.empty((M, N), dtype=torch.int32, device=self.dev)
+            rmo = torch.zeros((M,), dtype=torch.int32, device=self.dev)
+            run = lambda: self.ok(L.ref_gemm_x32(P(X), K, P(rm), K, M, M, P(W), K, N, N, K, P(cst), P(Y), N, P(R), 0, None, P(rmo)))
+        else:
+            q = self.ri(g, -32768, 32768, (M, K)); hi, lo = (q >> 8).to(torch.int8), ((q & 255) - 128).to(torch.int8); e = self.ri(g, 0, 6, (M,))
+            if kind == "geglu":
+                from math import erf, sqrt
+                xs = np.arange(2049, dtype=np.float64) / 64.0 - 16.0
+                Lphi = torch.from_numpy(np.rint([65536.0 * 0.5 * (1 + erf(x / sqrt(2))) for x in xs]).astype(np.int32)).to(self.dev)
+                Y = torch.empty((M, N // 2), dtype=torch.int32, device=self.dev); rmo = torch.zeros((M,), dtype=torch.int32, device=self.dev)
+                run = lambda: self.ok(L.ref_gemm_hl(P(hi), P(lo), K, M, M, P(W), K, N, N, K, P(cst), P(e), P(Y), N // 2, None, 2, 0, None, None, P(Lphi), P(rmo)))
+            else:
+                heads, T, C = 5, 4096, 320
+                G, Tp = (M // T) * heads, T
+                z = lambda *s, dt: torch.zeros(s, dtype=dt, device=self.dev)
+                qb = [z(G, Tp, 64, dt=torch.int8), z(G, Tp, 64, dt=torch.int8), z(G, Tp, dt=torch.int32)] + [z(G, Tp, dt=torch.int64) for _ in range(3)]
+                kb = [z(G, Tp, 64, dt=torch.int8), z(G, Tp, 64, dt=torch.int8), z(G, Tp, dt=torch.int32)] + [z(G, Tp, dt=torch.int64) for _ in range(3)]
+                V = z(M, C, dt=torch.int32)
+                run = lambda: self.ok(L.ref_gemm_qkv(P(hi), P(lo), K, P(e), M, M, P(W), K, N, N, K, P(cst), heads, T, Tp, Tp, C,
+                                                     *[P(x) for x in qb], *[P(x) for x in kb], P(V)))
+        ms = self.time(run)
+        return {"kernel": f"reference gemm_hl {kind} (64x64 level)", "M": M, "N": N, "K": K, "ms": round(ms, 4), "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
 
 
 # ------------------------------------------------------------------ CPU baseline (the oracle, bounded sample)
@@ -678,6 +872,24 @@ def run_reference(a, R):
 def run_kernel(a, R):
     import torch
     dev = torch.device("cuda", R.local)
+    if a.impl == "reference":
+        K = RefKernels(dev)
+        if a.kernel == "attention":
+            rep = K.attention()
+        elif a.kernel == "gemm":
+            rep = K.gemm()
+        elif a.kernel == "norms":
+            rep = K.norms()
+        elif a.kernel in ("linear", "geglu", "qkv"):
+            rep = K.linear(a.kernel, a.linear_k if a.kernel == "linear" else 320)
+        else:
+            rep = K.gn_conv(a.conv_level)
+        torch.cuda.synchronize()
+        rep["impl"] = "reference"
+        rep["native_libs"] = loaded_native_libs()
+        if R.rank == 0:
+            print(json.dumps(rep), flush=True)
+        return
     if a.kernel == "attention":
         case = AttentionCase(dev)
         for _ in range(3):
@@ -689,7 +901,7 @@ def run_kernel(a, R):
     elif a.kernel == "norms":
         case = GnConvCase(dev, 0)
         rep = case.report_norms()
-    elif a.kernel in ("linear", "geglu"):
+    elif a.kernel in ("linear", "geglu", "qkv"):
         case = LinearCase(dev, a.kernel, a.linear_k if a.kernel == "linear" else 320)
         rep = case.report()
     else:

@@ -29,10 +29,12 @@
 using namespace meow;
 
 static thread_local std::string g_err;
-#define GUARD(...) try { __VA_ARGS__; CUDA_CHECK(cudaDeviceSynchronize()); CUDA_CHECK(cudaGetLastError()); return 0; } \
+static thread_local bool g_sync = true;      // false: launches return without waiting (timing loops)
+#define GUARD(...) try { __VA_ARGS__; if (g_sync) CUDA_CHECK(cudaDeviceSynchronize()); CUDA_CHECK(cudaGetLastError()); return 0; } \
                     catch (const std::exception& ex) { g_err = ex.what(); return -1; }
 
 extern "C" const char* ref_last_error() { return g_err.c_str(); }
+extern "C" void ref_set_sync(int sync) { g_sync = sync != 0; }
 
 // ------------------------------------------------------------------ operators (src/kernels.h, src/gemm_hl.h)
 extern "C" int ref_quant_rows(const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
