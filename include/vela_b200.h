@@ -51,7 +51,7 @@ unsigned vela_device_error(int clear);
  * ------------------------------------------------------------------------------ */
 #define VELA_SRC_I8      0     /* planar int8 hi/lo rows + per-row e */
 #define VELA_SRC_X32     1     /* int32 rows quantised on load with e = row_exp(rowmax[row]) */
-#define VELA_SRC_CONV32  2     /* NHWC int32 image, implicit 3x3 pad-1 im2col, K = 9C tap-major, e from vela_conv_e */
+#define VELA_SRC_CONV32  2     /* NHWC int32 image, implicit 3x3 pad-1 im2col, K = 9C tap-major (C % 32 == 0 or C == 4), e from vela_conv_e */
 #define VELA_EPI_PLAIN   0     /* y (+ residual), optional per-row max |y| */
 #define VELA_EPI_SPLIT3  1     /* column n -> (Y | Y1 | Y2)[row][n % Cs] */
 #define VELA_EPI_GEGLU   2     /* interleaved a|g columns: Y[row][c] = a * GELU(g) / 2^16, optional row max */

@@ -70,7 +70,7 @@ def test_gemm_rejects_bad_arguments(case):
 def test_attention_rejects_bad_shapes():
     L = V.lib()
     p = ctypes.c_void_p(16)
-    # Tqp not a multiple of 128
+    # Tqp not a multiple of 64
     rc = L.vela_fused_attention(None, p, p, p, p, p, p, p, p, p, p, p, p, p, 1, 1, 100, 100, 64, 64, 0, p, 64, None, None, p, p)
     assert rc == -1 and L.vela_last_error().decode()
 

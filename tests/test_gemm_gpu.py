@@ -144,6 +144,19 @@ def test_conv_320ch_16x16():
         assert np.array_equal(got, exp), stride
 
 
+@pytest.mark.parametrize("B,Hh,N", [(2, 64, 320), (3, 10, 64)])
+def test_conv_4ch_input(B, Hh, N):
+    """the UNet's input conv (4 channels, K = 36 padded to 48): nine 16-byte pixels per row quantised on load, no im2col
+    buffer; stride 1 and 2, full-range random bit widths"""
+    rng = np.random.default_rng(B * 10 + Hh); d = Dev()
+    X = rbits(rng, (B, Hh, Hh, 4), 30)
+    W = rng.integers(-127, 128, (N, 36)).astype(np.int8)
+    c = cst_for(rng, W, N, N)
+    for stride in (1, 2):
+        got, exp = conv_case(d, X, W, c, stride, Kp=48)
+        assert np.array_equal(got, exp), (B, Hh, N, stride)
+
+
 @pytest.mark.parametrize("B,Hh,C,N", [(2, 12, 64, 128), (3, 8, 96, 64), (1, 32, 64, 192)])
 def test_conv_shapes_both_loaders(B, Hh, C, N):
     """image sizes whose 128-row tiles are not whole output rows (12x12, stride-2 6x6) keep the per-thread loader;

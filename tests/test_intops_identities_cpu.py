@@ -12,7 +12,8 @@ kernel computes and checks it against the spec form on edge values and seeded ra
 - norm_val (rowops.cu): the binary64 quotient formed with the 1.5 * 2^52 constant and one fma residual test
   ==  floor((d 2^(25-e) + sd) / (2 sd));
 - the attention softmax forms (attn.cu): the 32-bit score (hh M + (T >> a)) >> b, its mixed-exponent
-  variant, the exp table interpolated with one mad.hi, and P from the reciprocal's 32-bit halves;
+  variant, the exp-table index read from the quotient before its >> b, the table interpolated with one mad.hi, and
+  P from the reciprocal's 32-bit halves saturated by the packing instruction;
 - the int32 staging quantiser is covered by the GPU parity tests.
 """
 import random
@@ -274,8 +275,46 @@ def test_attention_exp_table_fast_form():
             assert exp_fast_model(z, L) == exp_lut_ref(z, L), z
 
 
+def exp_fast_d_model(d, b, L):
+    """attn.cu exp_fast_d on d (uint32): i = min(d >> (b + 10), 1024), f 2^21 = (d 2^(21 - b) mod 2^32) & (1023 << 21),
+    E = mad.hi.s32(2 D, f 2^21, L[i]) with the sentinel (0, 0) at 1024"""
+    i = min(d >> (b + 10), 1024)
+    F = (d * (1 << (21 - b))) & 0x7FE00000
+    Li, D2 = (L[i], 2 * (L[i + 1] - L[i])) if i < 1024 else (0, 0)
+    return s32(mulhi32(D2, F) + Li)
+
+
+def test_attention_exp_index_from_quotient():
+    """the exp-table index and fraction from d = mx 2^b + 2^b - 1 - u (mod 2^32), u the score before its >> b, equal the
+    table at z = mx - (u >> b) for every shift the fast path takes and every valid key (u >> b <= mx); the default table
+    also qualifies for the three-term 32-bit sums (every entry <= 2^32 / 3)"""
+    import math
+    rnd = random.Random(25)
+    L = [round(2**30 * math.exp(-i / 64.0)) for i in range(1025)]
+    assert max(L) <= 0x55555555 and 3 * max(L) < 2**32
+    for hh, xx, ll, kc, cq, S in _score_operands(rnd, 150):
+        for sh in range(5, 20):
+            a = min(sh, 16)
+            b = sh - a
+            T = 256 * xx + ll + kc + cq + (1 << (sh - 1))
+            u = s32(hh * (1 << (16 - a)) + (T >> a))
+            s = u >> b
+            if b > 0:
+                assert abs(u) < 2**21
+            for z in (0, 1, 1023, 1024, (1 << 20) - 1, 1 << 20, (1 << 20) + 3, rnd.randint(0, 1 << 21), rnd.randint(0, 1 << 20)):
+                mx = s + z
+                if mx > INT_MAX:
+                    continue
+                mxb = (mx << b) + (1 << b) - 1
+                assert b == 0 or INT_MIN <= mxb <= INT_MAX
+                d = (mxb - u) & 0xFFFFFFFF
+                assert exp_fast_d_model(d, b, L) == exp_lut_ref(z, L), (sh, z)
+
+
 def test_attention_p_short_form():
-    """P = min(32767, (E r + 2^46) >> 47) with r = floor(2^62 / sum E) == min(32767, (E rhi + hi32(E rlo) + 2^14) >> 15)"""
+    """P = min(32767, (E r + 2^46) >> 47) with r = floor(2^62 / sum E) == sat16((E rhi + hi32(E rlo) + 2^14) >> 15), the
+    saturation being that of cvt.pack.sat.s16.s32 (the value is below 2^17); sum P is read from the P.V products as
+    256 sum ph + sum pl + 128 n (the plane-sum identity of test_plane_sums, padded keys carrying P = 0)"""
     rnd = random.Random(24)
     for _ in range(3000):
         n = rnd.randint(1, 4096)
@@ -288,4 +327,8 @@ def test_attention_p_short_form():
         for E in Es:
             want = min(32767, (E * r + (1 << 46)) >> 47)
             h = (E * rhi + ((E * rlo) >> 32) + 16384) & 0xFFFFFFFF
-            assert min(h >> 15, 32767) == want
+            assert h >> 15 < 2**17 and pack_sat16(h >> 15) == want
+    # a single key carries the whole sum: P = 32768 before the clamp
+    r = (1 << 62) // (2**30)
+    h = (2**30 * (r >> 32) + ((2**30 * (r & 0xFFFFFFFF)) >> 32) + 16384) & 0xFFFFFFFF
+    assert h >> 15 == 32768 and pack_sat16(h >> 15) == 32767

@@ -17,16 +17,21 @@
 //       P = 256 ph + pl + 128 with ph = P >> 8, pl = (P & 255) - 128 written to shared memory by the
 //       softmax warps as the A operand; A = Ph.Vh, Y = Ph.Vl + Pl.Vh, D = Pl.Vl (K-major V^T tiles);
 //       n = number of keys swept (padded keys carry V = 0 and P = 0).
+//     sum_k P comes from the tensor core too: the V^T tiles have 16 constant rows below the 64 dims (N = 80), row 64
+//       of the lo plane all ones and the rest zero, so column 64 holds Y = sum ph and D = sum pl, and
+//       sum P = 256 Y + D + 128 n.
 // Softmax arithmetic per score element (the CUDA-core work that bounds the kernel): the score in 32-bit wrapping
-// arithmetic as (hh M + (T >> a)) >> b (see div_pow2), the exp table interpolated with one mad.hi on entries
-// (L[i], 2 (L[i+1] - L[i])), and P from two multiply-adds of E with the 64-bit reciprocal's halves; the integer work is
-// split between the ALU and FMA pipes.  A per-stage aux warp turns each K tile's ksum into int32 and the 16-key
-// quarters' exponent ranges once per CTA, so the softmax warps only read them.
+// arithmetic as hh M + (T >> a) (see div_pow2), the exp-table index and fraction taken from mx 2^b - that quotient
+// without forming the score itself (see exp_fast_d), the table interpolated with one mad.hi on entries
+// (L[i], 2 (L[i+1] - L[i])), and P from two multiply-adds of E with the 64-bit reciprocal's halves, saturated to
+// 32767 by the packing instruction; the integer work is split between the ALU and FMA pipes.  A per-stage aux warp
+// turns each K tile's ksum into int32 and classifies the 16-key quarters (exponent form, masking) once per CTA, so
+// the softmax warps read one word per tile.
 // Warp roles: warp 0 TMA (Q once; K tiles + per-key ek/ksum each pass; V^T tiles in pass 2),
 // warp 1 TMEM allocation + MMA issue, warp 18 per-stage key data, warps 2..17 softmax (thread = one query row = one TMEM
 // lane; the four warps of a lane quarter split each 64-key tile, and the output dims, in quarters).
 // TMEM: QK buffers at columns [0,192) and [192,384) (passes 0-1 alternate; pass 2 uses the first),
-// P.V accumulators at [192,384) during pass 2.  All barrier waits are bounded.
+// P.V accumulators A, Y, D at [192,272), [272,352), [352,432) during pass 2.  All barrier waits are bounded.
 #include "intops.cuh"
 #include "tc.cuh"
 #include "host_util.h"
@@ -44,7 +49,9 @@ constexpr int KS = 4, VS = 2;                         // K and V ring depths
 constexpr int Q_BYTES = 128 * 64;                     // one plane of the 128-query tile
 constexpr int KT_BYTES = 64 * 64;                     // one plane of a 64-key tile
 constexpr int KSTAGE = 2 * KT_BYTES;                  // K hi + lo
-constexpr int VSTAGE = 2 * KT_BYTES;                  // V^T hi + lo
+constexpr int PV_N = 80;                              // P.V MMA width: 64 output dims + 16 constant rows (sum P)
+constexpr int VT_BYTES = PV_N * 64;                   // one plane of a V^T tile: 64 dims from TMA, then the constant rows
+constexpr int VSTAGE = 2 * VT_BYTES;                  // V^T hi + lo
 constexpr int P_BYTES = 128 * 64;                     // one plane of P
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int OFF_Q = 0;
@@ -52,9 +59,14 @@ constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KS * KSTAGE;
 constexpr int OFF_P = OFF_V + VS * VSTAGE;
 constexpr int OFF_KAUX = OFF_P + 2 * P_BYTES;          // per K stage: ek int32[64], ksum int64[64] (TMA), then the aux
-constexpr int KAUX_TMA = 64 * 4 + 64 * 8;              // warp's kc int32[64] (= 128 ksum) and per 16-key quarter (min ek, max ek)
+constexpr int KAUX_TMA = 64 * 4 + 64 * 8;              // warp's kc int32[64] (= 128 ksum) and one info word per 16-key quarter
 constexpr int KAUX_KC = KAUX_TMA, KAUX_QI = KAUX_KC + 64 * 4;
-constexpr int KAUX_BYTES = KAUX_QI + 4 * 8;
+constexpr int KAUX_BYTES = KAUX_QI + 4 * 4;
+// quarter info word: bits 0-7 the largest key exponent, bits 8-9 the form (0: one exponent; 1: exponents differ;
+// 2: some shift of the CTA's rows falls outside [5, 19]), bit 10: every key valid (no causal mask, none past Tk)
+constexpr int QI_MODE = 8, QI_FULL = 1 << 10;
+// P.V accumulator columns in TMEM
+constexpr uint32_t PV_A = 192, PV_Y = PV_A + PV_N, PV_D = PV_Y + PV_N;
 constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025] exp table (see exp_fast / exp_general); entry 1024 = (0, 0)
 constexpr int SW = 16;                                 // softmax warps: four per TMEM lane quarter, 16 keys each
 constexpr int AUX_WARP = 2 + SW;                      // per K stage: kc and the quarters' exponent range, once per CTA
@@ -64,10 +76,11 @@ constexpr int OFF_BAR = OFF_RED + 4 * 128 * 8;
 constexpr int NBAR = 1 + 3 * KS + 2 * VS + 2 + 2 + 2 + 1;
 constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;
 constexpr int TMEM_COLS = 512;
+static_assert(PV_D + PV_N <= TMEM_COLS && OFF_V % 1024 == 0 && VT_BYTES % 1024 == 0 && KAUX_BYTES % 16 == 0, "layout");
 
 // Constants the softmax multiplies by, passed as kernel arguments so the compiler keeps the multiply forms on the FMA
-// pipe instead of turning them into shifts and adds on the ALU pipe: 1, 256, 2^21, 8.
-struct OpK { int c1, c256, c2p21, c8; };
+// pipe instead of turning them into shifts and adds on the ALU pipe: 256, 8.
+struct OpK { int c256, c8; };
 
 struct AttnArgs {
     CUtensorMap tmQh, tmQl, tmKh, tmKl, tmVh, tmVl;
@@ -80,7 +93,7 @@ struct AttnArgs {
     unsigned* err;
     long long wait_limit;          // SM clock cycles before a barrier wait gives up
     int stall;                     // failure-path tests: the TMA producer issues nothing
-    OpK k;                         // the constants 1, 256, 2^21 and 8 (see OpK)
+    OpK k;                         // the constants 256 and 8 (see OpK)
 };
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -118,23 +131,39 @@ __device__ __forceinline__ ShiftSplit split_shift(int sh) {
 __device__ __forceinline__ int div_pow2(int hh, int T, const ShiftSplit& p) { return mad_lo(hh, p.M, T >> p.a); }
 
 // ---- exp table: E = L[i] + floor((L[i+1] - L[i]) f / 2^10) for z = mx - s, i = min(z, 2^20) >> 10, f = its low 10 bits
-// (index 1024 is a sentinel (0, 0): E = 0 from z = 2^20 on).  Fast table (every L[i] in [0, 2^31) and every difference
-// below 2^30 in magnitude): entries (L[i], 2 (L[i+1] - L[i])) and E = hi32(2 D * f 2^21) + L[i] in one mad.hi.
-// General table: entries (L[i], L[i+1]) and the difference in 64 bits, exactly as the reference does.
-__device__ __forceinline__ uint32_t zclamp(int mx, int s) { return min(uint32_t(mx) - uint32_t(s), 1u << 20); }
-__device__ __forceinline__ int exp_fast(uint32_t zc, uint32_t lut_addr, const OpK& k) {
-    const int2 e = lds_v2(uint32_t(mad_lo(int(zc >> 10), k.c8, int(lut_addr))));
-    return mad_hi(e.y, mul_lo(int(zc & 1023u), k.c2p21), e.x);
+// (index 1024 is a sentinel (0, 0): E = 0 from z = 2^20 on).  Fast table (every L[i] in [0, 2^32 / 3], so three E add
+// up in 32 bits, and every difference below 2^30 in magnitude): entries (L[i], 2 (L[i+1] - L[i])) and
+// E = hi32(2 D * f 2^21) + L[i] in one mad.hi.  General table: entries (L[i], L[i+1]) and the difference in 64 bits,
+// exactly as the reference does.
+//
+// The fast form reads i and f without forming s or z.  With the score s = u >> b (u = hh M + (T >> a), b in [0, 3]) and
+// mxb = mx 2^b + 2^b - 1:  d = mxb - u >= 0 for every valid key and d >> b = mx - floor(u / 2^b) = z
+// (ceil((u - 2^b + 1) / 2^b) = floor(u / 2^b)), so i = min(d >> (b + 10), 1024) and f 2^21 = (d 2^(21 - b)) & (1023 << 21).
+// |u| < 2^21 when b > 0, so mx 2^b cannot wrap; with b = 0 the quotient is the score and d = z modulo 2^32.  An invalid
+// key's d is arbitrary, its index still lies in [0, 1024] and its E is masked afterwards.
+struct ExpIdx { int shi, mulf; };                          // b + 10 and 2^(21 - b)
+__device__ __forceinline__ ExpIdx exp_idx(int b) { return ExpIdx{b + 10, 1 << (21 - b)}; }
+__device__ __forceinline__ int exp_fast_d(uint32_t d, const ExpIdx& x, uint32_t lut_addr, const OpK& k) {
+    const uint32_t i = min(d >> x.shi, 1024u);
+    const int2 e = lds_v2(uint32_t(mad_lo(int(i), k.c8, int(lut_addr))));
+    return mad_hi(e.y, int(uint32_t(mul_lo(int(d), x.mulf)) & 0x7FE00000u), e.x);
 }
+__device__ __forceinline__ uint32_t zclamp(int mx, int s) { return min(uint32_t(mx) - uint32_t(s), 1u << 20); }
 __device__ __forceinline__ int exp_general(uint32_t zc, const int2* __restrict__ T) {
     const int2 e = T[zc >> 10];
     return int(i64(e.x) + (((i64(e.y) - e.x) * int(zc & 1023u)) >> 10));
 }
-// P = min(32767, (E r + 2^46) >> 47) for 0 <= E <= sum E, r = floor(2^62 / sum E) = rhi 2^32 + rlo: E r <= 2^62, so
-// floor((E r + 2^46) / 2^47) = floor((E rhi + hi32(E rlo) + 2^14) / 2^15), every term below 2^32.
+// P before the 32767 clamp: (E r + 2^46) >> 47 for 0 <= E <= sum E, r = floor(2^62 / sum E) = rhi 2^32 + rlo: E r <= 2^62,
+// so floor((E r + 2^46) / 2^47) = floor((E rhi + hi32(E rlo) + 2^14) / 2^15), every term below 2^32, the result below
+// 2^17.  The clamp is the saturation of the packing instruction (pack_sat2).
 __device__ __forceinline__ int p_of(uint32_t E, uint32_t rlo, uint32_t rhi) {
-    const uint32_t h = mad_lo_u(E, rhi, mad_hi_u(E, rlo, 16384u));
-    return int(min(h >> 15, 32767u));
+    return int(mad_lo_u(E, rhi, mad_hi_u(E, rlo, 16384u)) >> 15);
+}
+// two non-negative values saturated to 32767 and packed as 16-bit halves (hi, lo)
+__device__ __forceinline__ uint32_t pack_sat2(int hi, int lo) {
+    uint32_t w;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(w) : "r"(hi), "r"(lo));
+    return w;
 }
 // the same for any table: E may be negative; the reference's int64 arithmetic with P = 0 unless E > 0
 __device__ __forceinline__ int p_general(int E, uint64_t r) {
@@ -154,17 +183,24 @@ struct RowK { int shq, cq, r0; };
 template <int PASS, bool TF, bool FULL>
 __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restrict__ ekp, const int* __restrict__ kcp, const RowK& rk, int mode, int eku,
                                              int kbase, int q, int Tk, int causal, const int2* __restrict__ L2, uint32_t lut_addr, const OpK& k,
-                                             int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, int& psum, uint32_t* pw_h, uint32_t* pw_l,
+                                             int& mx, uint64_t& sum, uint32_t rlo, uint32_t rhi, uint32_t* pw_h, uint32_t* pw_l,
                                              uint64_t* rel_qk) {
     int s[16];
     bool pre_shift = false;          // PASS 0, mode 0: s holds hh M + (T >> a); the row max takes the >> b once per chunk
     int bsh = 0;
+    // passes 1-2 with the fast table: s holds u (mode 0: before the >> b) and the exp index comes from mxb - u
+    uint32_t mxb = uint32_t(mx);
+    ExpIdx xi = exp_idx(0);
     const ShiftSplit p = split_shift(mode == 2 ? 16 : rk.shq - eku);
     // X and LL first, folded into T (16 registers), then HH: the three accumulators are never all live at once
+    int hh[16];
     {
         int xx[16], ll[16];
-        tmem_ld16(taddr + 64, xx); tmem_ld16(taddr + 128, ll);
+        tmem_ld16(taddr + 64, xx); tmem_ld16(taddr + 128, ll); tmem_ld16(taddr, hh);
         tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(rel_qk);
         if (mode == 0) {
             const int cr = rk.cq + (1 << (rk.shq - eku - 1));
             #pragma unroll
@@ -189,19 +225,11 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
         }
     }
     {
-        int hh[16];
-        tmem_ld16(taddr, hh);
-        tmem_ld_wait();
-        // every accumulator of the tile is in registers: hand the QK buffer back now, so the next tile's QK products
-        // run on the tensor core while this tile's arithmetic runs here (the K stage, whose per-key data is still
-        // read below, is handed back by the caller)
-        tc_fence_before();
-        __syncwarp();
-        if ((threadIdx.x & 31) == 0) mbar_arrive(rel_qk);
         if (mode == 0) {
             #pragma unroll
             for (int u = 0; u < 16; ++u) s[u] = div_pow2(hh[u], s[u], p);
             if (PASS == 0 && FULL) { pre_shift = true; bsh = p.b; }
+            else if (PASS >= 1 && TF) { xi = exp_idx(p.b); mxb = (uint32_t(mx) << p.b) + ((1u << p.b) - 1u); }
             else if (__any_sync(0xffffffffu, p.b != 0)) {
                 #pragma unroll
                 for (int u = 0; u < 16; ++u) s[u] >>= p.b;
@@ -241,13 +269,16 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
         }
     } else if constexpr (PASS == 1) {
         if constexpr (TF) {
-            // each E < 2^31: a pair fits 32 bits (added on the FMA pipe), then to the 64-bit sum on the ALU pipe
+            // each E <= 2^32 / 3: three add up in 32 bits (one three-input add), then to the 64-bit sum
+            uint32_t e[16];
             #pragma unroll
-            for (int u = 0; u < 16; u += 2) {
-                int e0 = exp_fast(zclamp(mx, s[u]), lut_addr, k), e1 = exp_fast(zclamp(mx, s[u + 1]), lut_addr, k);
-                if (!FULL) { e0 = (vmask >> u) & 1u ? e0 : 0; e1 = (vmask >> (u + 1)) & 1u ? e1 : 0; }
-                sum += uint32_t(mad_lo(e0, k.c1, e1));
+            for (int u = 0; u < 16; ++u) {
+                e[u] = uint32_t(exp_fast_d(mxb - uint32_t(s[u]), xi, lut_addr, k));
+                if (!FULL) e[u] = (vmask >> u) & 1u ? e[u] : 0u;
             }
+            #pragma unroll
+            for (int u = 0; u < 15; u += 3) sum += e[u] + e[u + 1] + e[u + 2];
+            sum += e[15];
         } else {
             #pragma unroll
             for (int u = 0; u < 16; ++u) {
@@ -261,13 +292,12 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, const int* __restri
             int P[4];
             #pragma unroll
             for (int w = 0; w < 4; ++w) {
-                if constexpr (TF) P[w] = p_of(uint32_t(exp_fast(zclamp(mx, s[u + w]), lut_addr, k)), rlo, rhi);
+                if constexpr (TF) P[w] = p_of(uint32_t(exp_fast_d(mxb - uint32_t(s[u + w]), xi, lut_addr, k)), rlo, rhi);
                 else P[w] = p_general(exp_general(zclamp(mx, s[u + w]), L2), (uint64_t(rhi) << 32) | rlo);
                 if (!FULL) P[w] = (vmask >> (u + w)) & 1u ? P[w] : 0;
-                psum = mad_lo(P[w], k.c1, psum);
             }
-            // 0 <= P < 2^15: the four 16-bit values as two words, then their hi bytes and (lo bytes - 128)
-            const uint32_t w01 = __byte_perm(uint32_t(P[0]), uint32_t(P[1]), 0x5410), w23 = __byte_perm(uint32_t(P[2]), uint32_t(P[3]), 0x5410);
+            // 0 <= P < 2^17, saturated to 32767 while packed as 16-bit halves; then the hi bytes and (lo bytes - 128)
+            const uint32_t w01 = pack_sat2(P[1], P[0]), w23 = pack_sat2(P[3], P[2]);
             pw_h[u / 4] = __byte_perm(w01, w23, 0x7531);
             pw_l[u / 4] = __byte_perm(w01, w23, 0x6420) ^ 0x80808080u;
         }
@@ -283,9 +313,9 @@ struct SoftCtx {
     uint8_t *pst_h, *pst_l;         // this thread's 16 P bytes in the hi / lo P tiles (pass 2)
     uint32_t tq;                    // TMEM address of this thread's lane quarter and key quarter in QK buffer 0
     RowK rk;
-    int shq_min, kq, q, nT;
+    int kq, q, nT;
 };
-struct SoftState { int mx; uint64_t sum; uint32_t rlo, rhi; int psum; bool ok; };
+struct SoftState { int mx; uint64_t sum; uint32_t rlo, rhi; bool ok; };
 
 // One pass over every key tile for this thread's row and key quarter.  Every warp runs every iteration, also after
 // a timed-out wait (it then skips the work), so the barriers' arrival counts stay consistent.
@@ -293,25 +323,24 @@ template <int PASS, bool TF>
 __device__ __forceinline__ void softmax_pass(const AttnArgs& a, const SoftCtx& c, SoftState& st) {
     const int lane = threadIdx.x & 31;
     for (int j = 0; j < c.nT; ++j) {
-        const int it = PASS * c.nT + j, ks = it % KS;
-        const int b = PASS < 2 ? (it & 1) : 0;
-        const int ub = PASS < 2 ? (it >> 1) : it - c.nT;           // earlier uses of buffer b
-        if (st.ok) st.ok = __all_sync(0xffffffffu, mbar_wait(&c.qk_full[b], ub & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
-        if (st.ok) st.ok = __all_sync(0xffffffffu, mbar_wait(&c.kinfo_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
+        const unsigned it = unsigned(PASS * c.nT + j), ks = it % KS;
+        const unsigned b = PASS < 2 ? (it & 1u) : 0u;
+        const unsigned ub = PASS < 2 ? (it >> 1) : it - unsigned(c.nT);     // earlier uses of buffer b
+        if (st.ok) st.ok = __all_sync(0xffffffffu, mbar_wait(&c.qk_full[b], ub & 1u, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit) &&
+                                                   mbar_wait(&c.kinfo_full[ks], (it / KS) & 1u, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
         if (!st.ok) continue;
         tc_fence_after();
         const uint8_t* aux = c.kaux + ks * KAUX_BYTES;
-        const int2 qi = reinterpret_cast<const int2*>(aux + KAUX_QI)[c.kq];      // (min, max) key exponent of the quarter
+        const int info = reinterpret_cast<const int*>(aux + KAUX_QI)[c.kq];
+        const int eku = info & 255, mode = (info >> QI_MODE) & 3;
         const int kbase = j * 64 + c.kq * 16;
-        const bool full = !a.causal && kbase + 16 <= a.Tk;
-        const int mode = c.shq_min - qi.y < 5 ? 2 : (qi.x == qi.y ? 0 : 1);   // fast forms need every shift in [5, 19]
         uint32_t pw_h[4], pw_l[4];
         const int* ekp = reinterpret_cast<const int*>(aux) + c.kq * 16;
         const int* kcp = reinterpret_cast<const int*>(aux + KAUX_KC) + c.kq * 16;
-        if (full) softmax_tile<PASS, TF, true>(c.tq + uint32_t(b * 192), ekp, kcp, c.rk, mode, qi.y, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
-                                               st.mx, st.sum, st.rlo, st.rhi, st.psum, pw_h, pw_l, &c.qk_free[b]);
-        else softmax_tile<PASS, TF, false>(c.tq + uint32_t(b * 192), ekp, kcp, c.rk, mode, qi.y, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
-                                           st.mx, st.sum, st.rlo, st.rhi, st.psum, pw_h, pw_l, &c.qk_free[b]);
+        if (info & QI_FULL) softmax_tile<PASS, TF, true>(c.tq + b * 192u, ekp, kcp, c.rk, mode, eku, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
+                                                         st.mx, st.sum, st.rlo, st.rhi, pw_h, pw_l, &c.qk_free[b]);
+        else softmax_tile<PASS, TF, false>(c.tq + b * 192u, ekp, kcp, c.rk, mode, eku, kbase, c.q, a.Tk, a.causal, c.lut, c.lut_addr, a.k,
+                                           st.mx, st.sum, st.rlo, st.rhi, pw_h, pw_l, &c.qk_free[b]);
         bool pout = false;
         if (PASS == 2) {
             st.ok = __all_sync(0xffffffffu, mbar_wait(c.p_free, (j & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit));
@@ -358,7 +387,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         mbar_fence_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
-    // exp table: (L[i], L[i+1]) staged, and whether it qualifies for the fast form (every L[i] >= 0 and every
+    // exp table: (L[i], L[i+1]) staged, and whether it qualifies for the fast form (every L[i] in [0, 2^32 / 3] and every
     // difference below 2^30 in magnitude); then the fast form replaces L[i+1] by 2 (L[i+1] - L[i])
     int tf = 1;
     for (int i = threadIdx.x; i <= 1024; i += blockDim.x) {
@@ -366,10 +395,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         if (i < 1024) {
             v = make_int2(__ldg(a.lexp + i), __ldg(a.lexp + i + 1));
             const i64 d = i64(v.y) - v.x;
-            tf &= v.x >= 0 && v.y >= 0 && d < (i64(1) << 30) && d > -(i64(1) << 30);
+            tf &= v.x >= 0 && v.y >= 0 && v.x <= 0x55555555 && v.y <= 0x55555555 && d < (i64(1) << 30) && d > -(i64(1) << 30);
         }
         lut2[i] = v;
     }
+    // the constant rows 64..79 of every V^T stage: zero, except row 64 of the lo plane, all ones (16-byte chunks)
+    for (int i = threadIdx.x; i < VS * 2 * 64; i += blockDim.x) {
+        const int s = i >> 7, plane = (i >> 6) & 1, c = i & 63;
+        const uint32_t v = (plane == 1 && c < 4) ? 0x01010101u : 0u;
+        *reinterpret_cast<uint4*>(sm + OFF_V + s * VSTAGE + plane * VT_BYTES + KT_BYTES + c * 16) = make_uint4(v, v, v, v);
+    }
+    fence_async_smem();
     const bool tfast = __syncthreads_and(tf) != 0;
     if (tfast)
         for (int i = threadIdx.x; i < 1024; i += blockDim.x) lut2[i].y = 2 * (lut2[i].y - lut2[i].x);
@@ -397,34 +433,33 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 if (it >= 2 * nT) {
                     const int vs = j % VS;
                     if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, a.err, DEVERR_TIMEOUT_EMPTY, a.wait_limit)) break;
-                    mbar_arrive_expect_tx(&v_full[vs], VSTAGE);
+                    mbar_arrive_expect_tx(&v_full[vs], 2 * KT_BYTES);
                     uint8_t* vst = sm + OFF_V + vs * VSTAGE;
                     tma_load_2d(vst, &a.tmVh, &v_full[vs], j * 64, g * 64);
-                    tma_load_2d(vst + KT_BYTES, &a.tmVl, &v_full[vs], j * 64, g * 64);
+                    tma_load_2d(vst + VT_BYTES, &a.tmVl, &v_full[vs], j * 64, g * 64);
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_i8(128, 64);
+            constexpr uint32_t idesc = idesc_i8(128, 64), idesc_pv = idesc_i8(128, PV_N);
             const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + Q_BYTES;
             const uint32_t ph = smem_u32(sm + OFF_P), pl = ph + P_BYTES;
-            const uint32_t pv = tmem + 192;                   // A: [192,256), Y: [256,320), D: [320,384)
             bool ok = mbar_wait(q_full, 0, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit);
             auto issue_pv = [&](int j) -> bool {
                 const int vs = j % VS;
                 if (!mbar_wait(p_full, j & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) return false;
                 if (!mbar_wait(&v_full[vs], (j / VS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit)) return false;
                 tc_fence_after();
-                const uint32_t vh = smem_u32(sm + OFF_V + vs * VSTAGE), vl = vh + KT_BYTES;
+                const uint32_t vh = smem_u32(sm + OFF_V + vs * VSTAGE), vl = vh + VT_BYTES;
                 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
                     const bool acc = (j | kk) != 0;
-                    mma_i8(pv, sdesc_sw64(ph + kk * 32), sdesc_sw64(vh + kk * 32), idesc, acc);
-                    mma_i8(pv + 64, sdesc_sw64(ph + kk * 32), sdesc_sw64(vl + kk * 32), idesc, acc);
-                    mma_i8(pv + 64, sdesc_sw64(pl + kk * 32), sdesc_sw64(vh + kk * 32), idesc, true);
-                    mma_i8(pv + 128, sdesc_sw64(pl + kk * 32), sdesc_sw64(vl + kk * 32), idesc, acc);
+                    mma_i8(tmem + PV_A, sdesc_sw64(ph + kk * 32), sdesc_sw64(vh + kk * 32), idesc_pv, acc);
+                    mma_i8(tmem + PV_Y, sdesc_sw64(ph + kk * 32), sdesc_sw64(vl + kk * 32), idesc_pv, acc);
+                    mma_i8(tmem + PV_Y, sdesc_sw64(pl + kk * 32), sdesc_sw64(vh + kk * 32), idesc_pv, true);
+                    mma_i8(tmem + PV_D, sdesc_sw64(pl + kk * 32), sdesc_sw64(vl + kk * 32), idesc_pv, acc);
                 }
                 mma_commit(p_free);
                 mma_commit(&v_empty[vs]);
@@ -459,17 +494,27 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         }
     } else if (warp == AUX_WARP) {
         // ---------------------------------------------------------------- per-stage key data, once per CTA
-        // kc = 128 ksum as int32 (|ksum| <= 64 * 32767) and the (min, max) exponent of each 16-key quarter
+        // kc = 128 ksum as int32 (|ksum| <= 64 * 32767) and each 16-key quarter's info word: its largest key exponent,
+        // the score form and whether every key is valid.  The fast forms need every shift 19 - eq - ek of the CTA's
+        // rows in [5, 19], checked against the CTA's largest row exponent (rows past Tqp do not exist).
+        int eqmax = 0;
+        for (int r = lane; r < 128; r += 32)
+            if (q0 + r < a.Tqp) eqmax = max(eqmax, __ldg(a.eq + size_t(g) * a.Tqp + q0 + r));
+        const int shq_min = 19 - __reduce_max_sync(0xffffffffu, eqmax);
+        auto info_word = [&](int emin, int emax, int kbase) {
+            const int mode = shq_min - emax < 5 ? 2 : (emin == emax ? 0 : 1);
+            return emax | (mode << QI_MODE) | (!a.causal && kbase + 16 <= a.Tk ? QI_FULL : 0);
+        };
         bool ok = true;
         for (int it = 0; it < nIt && ok; ++it) {
-            const int ks = it % KS;
+            const int ks = it % KS, j = it % nT;
             ok = __all_sync(0xffffffffu, mbar_wait(&k_full[ks], (it / KS) & 1, a.err, DEVERR_TIMEOUT_FULL, a.wait_limit));
             if (!ok) break;
             uint8_t* aux = sm + OFF_KAUX + ks * KAUX_BYTES;
             const int32_t* ek = reinterpret_cast<const int32_t*>(aux);
             const i64* ksum = reinterpret_cast<const i64*>(aux + 256);
             int32_t* kc = reinterpret_cast<int32_t*>(aux + KAUX_KC);
-            int2* qi = reinterpret_cast<int2*>(aux + KAUX_QI);
+            int* qi = reinterpret_cast<int*>(aux + KAUX_QI);
             const int e0 = ek[lane], e1 = ek[lane + 32];            // quarters lane >> 4 and 2 + (lane >> 4)
             kc[lane] = int(128 * ksum[lane]); kc[lane + 32] = int(128 * ksum[lane + 32]);
             int mn0 = e0, mx0 = e0, mn1 = e1, mx1 = e1;
@@ -478,7 +523,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
                 mn0 = min(mn0, __shfl_xor_sync(0xffffffffu, mn0, o)); mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
                 mn1 = min(mn1, __shfl_xor_sync(0xffffffffu, mn1, o)); mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
             }
-            if ((lane & 15) == 0) { qi[lane >> 4] = make_int2(mn0, mx0); qi[2 + (lane >> 4)] = make_int2(mn1, mx1); }
+            if ((lane & 15) == 0) {
+                const int k0 = lane >> 4;
+                qi[k0] = info_word(mn0, mx0, j * 64 + k0 * 16);
+                qi[2 + k0] = info_word(mn1, mx1, j * 64 + (2 + k0) * 16);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&kinfo_full[ks]);
         }
@@ -488,8 +537,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         const int rl = qq * 32 + lane, q = q0 + rl;
         const uint32_t tl = uint32_t(qq * 32) << 16;
         const size_t rq = size_t(g) * a.Tqp + q;
-        const int eqv = __ldg(a.eq + rq);
-        const int cq = int(32768 * __ldg(a.qhs + rq) + 128 * __ldg(a.qls + rq));
+        const bool qin = q < a.Tqp;                                 // the last query tile may reach past Tqp (Tqp % 128 == 64)
+        const int eqv = qin ? __ldg(a.eq + rq) : 0;
+        const int cq = qin ? int(32768 * __ldg(a.qhs + rq) + 128 * __ldg(a.qls + rq)) : 0;
         const int shq = 19 - eqv;                                   // eq <= 17, so shq >= 2
         SoftCtx c;
         c.qk_full = qk_full; c.qk_free = qk_free; c.k_empty = k_empty; c.kinfo_full = kinfo_full; c.p_full = p_full; c.p_free = p_free;
@@ -497,10 +547,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         c.pst_h = sm + OFF_P + sw64_off(rl, kq); c.pst_l = c.pst_h + P_BYTES;
         c.tq = tmem + tl + uint32_t(kq * 16);
         c.rk = RowK{shq, cq, 1 << (shq - 1)};                       // r0: rounding term of shift shq; >> ek gives that of shq - ek
-        c.shq_min = __reduce_min_sync(0xffffffffu, shq);
         c.kq = kq; c.q = q; c.nT = nT;
         i64* red = reinterpret_cast<i64*>(sm + OFF_RED);          // [4][128]
-        SoftState st{INT_MIN, 0, 0, 0, 0, true};
+        SoftState st{INT_MIN, 0, 0, 0, true};
         // combine the four key quarters of each row after pass 0 (max) and pass 1 (sum -> r)
         auto combine = [&](i64 v, i64* o) {
             red[kq * 128 + rl] = v;
@@ -522,23 +571,23 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         }
         if (tfast) softmax_pass<2, true>(a, c, st); else softmax_pass<2, false>(a, c, st);
         const bool ok = st.ok;
-        const int psum = st.psum;
         // ---------------------------------------------------------------- output
-        red[kq * 128 + rl] = psum;
-        asm volatile("bar.sync 1, %0;" :: "r"(SW * 32) : "memory");
-        const i64 ps = red[rl] + red[128 + rl] + red[256 + rl] + red[384 + rl];
         const bool done = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, 0, a.err, DEVERR_TIMEOUT_ACC, a.wait_limit));
         tc_fence_after();
         if (done) {
             const int bidx = g / a.heads, h = g % a.heads;
             const i64 n = a.Tkp;
+            // sum_k P = 256 sum ph + sum pl + 128 n from column 64 of the Y and D accumulators
+            int ysum, dsum;
+            tmem_ld1(tmem + tl + PV_Y + 64, &ysum); tmem_ld1(tmem + tl + PV_D + 64, &dsum);
             u32 am = 0;
             #pragma unroll
             for (int hv = 0; hv < 2; ++hv) {           // two halves of 8 output dims: fewer live registers
                 int A[8], Y[8], D[8];
-                const uint32_t col = uint32_t(192 + kq * 16 + hv * 8);
-                tmem_ld8(tmem + tl + col, A); tmem_ld8(tmem + tl + col + 64, Y); tmem_ld8(tmem + tl + col + 128, D);
+                const uint32_t col = uint32_t(kq * 16 + hv * 8);
+                tmem_ld8(tmem + tl + PV_A + col, A); tmem_ld8(tmem + tl + PV_Y + col, Y); tmem_ld8(tmem + tl + PV_D + col, D);
                 tmem_ld_wait();
+                const i64 ps = 256 * i64(ysum) + dsum + 128 * n;
                 if (q < a.Tq) {
                     int o[8];
                     #pragma unroll
@@ -585,7 +634,7 @@ void fused_attention(cudaStream_t st, const int8_t* qhi, const int8_t* qlo, cons
     a.err = o.err ? o.err : device_error_word(&g_attn_err);
     a.wait_limit = o.wait_limit > 0 ? o.wait_limit : WAIT_LIMIT_CYCLES;
     a.stall = o.stall;
-    a.k = OpK{1, 256, 1 << 21, 8};
+    a.k = OpK{256, 8};
     static std::atomic<int> attr_done[64];
     once_per_device(attr_done, [] { VELA_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)); });
     attn_kernel<<<dim3(ceil_div(Tqp, 128), G), THREADS, SMEM, st>>>(a);

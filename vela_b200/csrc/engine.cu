@@ -8,7 +8,7 @@
 // src/engine.cu:491-574, the step and its pipeline :599-677 (forwardIO, graph per slot, submit / collect / run).
 // Differences by design:
 //   - every GEMM, convolution (implicit 3x3, any depth) and attention runs on the tcgen05 kernels;
-//     no cuBLASLt, no im2col buffer (except the 4-channel input conv), no score buffers;
+//     no cuBLASLt, no im2col buffer, no score buffers;
 //   - weights are prepared once at load: 3x3 kernels permuted to tap-major K, N padded to 64,
 //     K to 16, q|k|v and the GEGLU a|g rows merged (a|g interleaved) exactly as the reference does;
 //   - the text encoder computes only the 77 real rows (every op on that path is row-local and the
@@ -621,20 +621,12 @@ private:
         const size_t mk = arena_.off;
         const uint32_t* pm = pmIn;
         if (!pm) { uint32_t* p = static_cast<uint32_t*>(arena_.alloc(size_t(x.B) * H * W * 4)); pixmax(st_, x.d, x.B * H * W, x.C, p); pm = p; }
-        if (x.C % 32 == 0) {
-            const int Mp = int(align_up(rows, 64));
-            int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
-            conv_e(st_, pm, x.B, H, W, stride, e);
-            vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_CONV32; A.img = x.d; A.H = H; A.W = W; A.C = x.C; A.stride = stride; A.Ho = Ho; A.Wo = Wo; A.K = L.K; A.e = e;
-            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
-        } else {       // 4-channel input image: explicit im2col (K = 36) then the planar GEMM
-            const int Mp = int(align_up(rows, 32));
-            int8_t* hi = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp)); int8_t* lo = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp));
-            int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
-            im2col3(st_, x.d, pm, x.B, H, W, x.C, stride, hi, lo, e, L.Kp);
-            vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;
-            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
-        }
+        // every depth, the 4-channel input image included, is quantised while loaded: no im2col buffer
+        const int Mp = int(align_up(rows, 64));
+        int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
+        conv_e(st_, pm, x.B, H, W, stride, e);
+        vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_CONV32; A.img = x.d; A.H = H; A.W = W; A.C = x.C; A.stride = stride; A.Ho = Ho; A.Wo = Wo; A.K = L.K; A.e = e;
+        gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
         arena_.off = mk;
         return y;
     }

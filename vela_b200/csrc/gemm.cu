@@ -47,8 +47,8 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 #define VELA_PERSIST_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm_persist<BN, ST, SRC, EPI>(const GemmArgs&, cudaStream_t);
 VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
 VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_SPLIT3) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_QKV)
-#define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 3, SRC, EPI_PLAIN) \
-    VELA_PERSIST_EXTERN(160, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(224, 3, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 3, SRC, EPI_PLAIN)
+#define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 4, SRC, EPI_PLAIN) \
+    VELA_PERSIST_EXTERN(160, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(224, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 4, SRC, EPI_PLAIN)
 VELA_PERSIST_REG(SRC_X32) VELA_PERSIST_REG(SRC_CONV32)
 
 namespace {
@@ -56,11 +56,11 @@ constexpr int REG_BNS[5] = {64, 128, 160, 224, 256};
 
 template <int SRC> void dispatch_reg(int BN, const GemmArgs& a, cudaStream_t st) {
     switch (BN) {
-        case 64: launch_gemm_persist<64, 3, SRC, EPI_PLAIN>(a, st); break;
-        case 128: launch_gemm_persist<128, 3, SRC, EPI_PLAIN>(a, st); break;
-        case 160: launch_gemm_persist<160, 3, SRC, EPI_PLAIN>(a, st); break;
-        case 224: launch_gemm_persist<224, 3, SRC, EPI_PLAIN>(a, st); break;
-        default: launch_gemm_persist<256, 3, SRC, EPI_PLAIN>(a, st); break;
+        case 64: launch_gemm_persist<64, 4, SRC, EPI_PLAIN>(a, st); break;
+        case 128: launch_gemm_persist<128, 4, SRC, EPI_PLAIN>(a, st); break;
+        case 160: launch_gemm_persist<160, 4, SRC, EPI_PLAIN>(a, st); break;
+        case 224: launch_gemm_persist<224, 4, SRC, EPI_PLAIN>(a, st); break;
+        default: launch_gemm_persist<256, 4, SRC, EPI_PLAIN>(a, st); break;
     }
 }
 
@@ -141,7 +141,8 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
         a.tmX = tmap2d(A.x, CU_TENSOR_MAP_DATA_TYPE_INT32, uint64_t(A.K), uint64_t(Mreal), uint64_t(A.ldx) * 4, 32, 128, Swz::B128);
         a.xtma = 1;
     } else if (src == VELA_SRC_CONV32) {
-        VELA_REQUIRE(A.img && A.e && A.C % 32 == 0 && A.K == 9 * A.C && A.K <= Kp && A.stride >= 1, "gemm: conv source needs C % 32 == 0, K = 9C");
+        VELA_REQUIRE(A.img && A.e && (A.C % 32 == 0 || A.C == 4) && A.K == 9 * A.C && A.K <= Kp && A.stride >= 1,
+                     "gemm: conv source needs C % 32 == 0 or C == 4, K = 9C");
         VELA_REQUIRE(A.Ho == (A.H - 1) / A.stride + 1 && A.Wo == (A.W - 1) / A.stride + 1, "gemm: conv output size");
         VELA_REQUIRE((reinterpret_cast<uintptr_t>(A.img) & 15) == 0, "gemm: image must be 16-byte aligned");
         a.img = A.img; a.H = A.H; a.W = A.W; a.C = A.C; a.stride = A.stride; a.Ho = A.Ho; a.Wo = A.Wo; a.K = A.K; a.e = A.e;
@@ -149,12 +150,12 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
         // read the NHWC box starting at (c0, kx - 1, oy0*s + ky - 1, b0) with element strides (1, s, s, 1); the
         // padding ring (coordinates -1 and past the edge) reads zeros.  Tiles must be whole output rows of one
         // image (Ho*Wo % 128 == 0 and 128 % Wo == 0) or whole images (128 % (Ho*Wo) == 0); other shapes keep
-        // the per-thread loads.
+        // the per-thread loads, and so does the 4-channel input image (nine 16-byte pixels per row in one k-block).
         const int howo = A.Ho * A.Wo, s = A.stride;
         int bw = 0, bh = 0, bb = 0;
         if (howo % 128 == 0 && 128 % A.Wo == 0) { bw = A.Wo * s; bh = (128 / A.Wo) * s; bb = 1; }
         else if (128 % howo == 0) { bw = A.Wo * s; bh = A.Ho * s; bb = 128 / howo; }
-        if (bw > 0 && bw <= 256 && bh <= 256 && s <= 8) {
+        if (A.C % 32 == 0 && bw > 0 && bw <= 256 && bh <= 256 && s <= 8) {
             const int Bimg = ceil_div(Mreal, howo);
             a.tmX = tmap_nhwc(A.img, uint64_t(Bimg), uint64_t(A.H), uint64_t(A.W), uint64_t(A.C), 32, uint32_t(bw), uint32_t(bh), uint32_t(bb),
                               uint32_t(s), Swz::B128);

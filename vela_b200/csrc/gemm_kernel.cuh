@@ -47,13 +47,17 @@ struct GemmArgs {
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }
 
+// An epilogue warp's shared-memory boxes for the TMA stores of Y: n (1 or 2) boxes of 2 KB from base, used in turn;
+// i counts the stores issued so far (null base: no TMA stores).
+struct YBox { uint8_t* base; int n; int i; };
+
 // Epilogue of one 128 x BN tile for one thread = one output row (rl) and the NC columns [c0, c0 + NC) of the tile
 // (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
 // applies the per-column constants (cst[j] = column n0 + j) and writes the epilogue's outputs.  er is the row's
 // exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory).
 template <int BN, int SRC, int EPI, int NC, bool FAST>
 __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                int m0, int n0, int rl, int c0, int split, int er, uint8_t* yb) {
+                                                int m0, int n0, int rl, int c0, int split, int er, YBox& yb) {
     static_assert(NC % 16 == 0, "16-column chunks");
     const int grow = m0 + rl;
     const bool live = grow < a.Mreal;
@@ -132,7 +136,7 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             int hi[16], lo[16];
             tmem_ld16(tl + col, hi); tmem_ld16(tl + BN + col, lo); tmem_ld_wait();
             // a TMA-stored plain chunk is written by the whole warp (rows past Mreal are clipped by the store)
-            const bool tstore = EPI == EPI_PLAIN && yb != nullptr;
+            const bool tstore = EPI == EPI_PLAIN && yb.base != nullptr;
             if (!act && !tstore) continue;
             if (a.partial) {             // split-K: raw accumulators, reduced by gemm_splitk_reduce
                 int32_t* ph = a.partial + (size_t(split) * 2 * a.Mp + grow) * a.Np + n;
@@ -147,8 +151,9 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             if constexpr (EPI == EPI_PLAIN) {
                 // four columns at a time: y, GELU, + residual, then out (shared-memory box or global) and the row max
                 const int lane = rl & 31;
-                if (tstore) {                            // the previous TMA store has finished reading the box
-                    if (lane == 0) bulk_wait_read0();
+                uint8_t* box = yb.base + (yb.i & (yb.n - 1)) * 2048;
+                if (tstore) {                            // the store that last used this box has finished reading it
+                    if (lane == 0) { if (yb.n == 2) bulk_wait_read1(); else bulk_wait_read0(); }
                     __syncwarp();
                 }
                 const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
@@ -176,7 +181,7 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                         }
                     }
                     if (tstore) {
-                        *reinterpret_cast<int4*>(yb + sw64_off(lane, g4)) = make_int4(y4[0], y4[1], y4[2], y4[3]);
+                        *reinterpret_cast<int4*>(box + sw64_off(lane, g4)) = make_int4(y4[0], y4[1], y4[2], y4[3]);
                     } else if (full16 && (a.ldy & 3) == 0) {
                         *reinterpret_cast<int4*>(dst + 4 * g4) = make_int4(y4[0], y4[1], y4[2], y4[3]);
                     } else {
@@ -191,7 +196,8 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                 if (tstore) {                            // the warp's 32 rows x 16 columns: one TMA store (rows past Mreal clipped)
                     fence_async_smem();
                     __syncwarp();
-                    if (lane == 0) { tma_store_2d(&a.tmY, yb, n, m0 + (rl & ~31)); bulk_commit(); }
+                    if (lane == 0) { tma_store_2d(&a.tmY, box, n, m0 + (rl & ~31)); bulk_commit(); }
+                    ++yb.i;
                 }
             } else {
                 int y[16];
@@ -232,12 +238,12 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
 // common path)
 template <int BN, int SRC, int EPI, int NC>
 __device__ __noinline__ void gemm_epilogue_general(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                   int m0, int n0, int rl, int c0, int split, int er, uint8_t* yb) {
+                                                   int m0, int n0, int rl, int c0, int split, int er, YBox& yb) {
     gemm_epilogue_t<BN, SRC, EPI, NC, false>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }
 template <int BN, int SRC, int EPI, int NC>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                              int m0, int n0, int rl, int c0, int split, int er, bool fast, uint8_t* yb) {
+                                              int m0, int n0, int rl, int c0, int split, int er, bool fast, YBox& yb) {
     if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
     else gemm_epilogue_general<BN, SRC, EPI, NC>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }

@@ -44,10 +44,17 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static constexpr bool SLUT = !REG;                          // GELU table staged in shared memory
     static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [2][BN] column constants (double-buffered by tile)
     static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[LUT_S_ENTRIES]
-    // plain epilogue: one 32 x 16 int32 box (2 KB, 64-byte swizzle) per epilogue warp for the TMA store of Y
-    static constexpr int YB_BYTES = EPI == EPI_PLAIN ? EW * 2048 : 0;
+    // plain epilogue: 32 x 16 int32 boxes (2 KB, 64-byte swizzle) per epilogue warp for the TMA stores of Y.  The
+    // wide int32-source tiles (several 16-column chunks per thread) take two boxes per warp, one filled while the
+    // other's store drains, where they fit without costing the staging ring a stage; the planar tiles (one chunk
+    // per thread and tile) keep one, which measured faster there.
+    static constexpr int YB_ONE = EPI == EPI_PLAIN ? EW * 2048 : 0;
     static constexpr int OFF_YB = (OFF_LUT + (SLUT ? LUT_S_ENTRIES * 8 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
+    static constexpr int XF1 = REG ? (227 * 1024 - 1024 - OFF_YB - YB_ONE) / X_STAGE : 0;
+    static constexpr int XF2 = REG ? (227 * 1024 - 1024 - OFF_YB - 2 * YB_ONE) / X_STAGE : 0;
+    static constexpr int YB_N = EPI == EPI_PLAIN && REG && (XF2 < 4 ? XF2 : 4) >= (XF1 < 4 ? XF1 : 4) ? 2 : 1;
+    static constexpr int YB_BYTES = YB_N * YB_ONE;
     static constexpr int OFF_X = OFF_YB + YB_BYTES;
     static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
     static constexpr int X_STAGES = X_FIT > 4 ? 4 : X_FIT;
@@ -212,6 +219,16 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
                     const uint8_t* xr = xstage + xs * Cfg::X_STAGE + half * Cfg::X_HALF + row * 128;
                     #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const int4*>(xr + ((j ^ (row & 7)) << 4));
+                } else if (SRC == SRC_CONV32 && a.C == 4) {
+                    // 4-channel image: the 32 K values are the taps k / 4 .. k / 4 + 7 of one 16-byte pixel each
+                    // (taps from 9 on are K padding and read as zero)
+                    const int tap0 = ((kb0 + i) * Cfg::BK + half * 32) >> 2;
+                    #pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int tap = tap0 + j, ky = tap / 3, kx = tap - ky * 3, iy = iy0 + ky, ix = ix0 + kx;
+                        v[j] = live && tap < 9 && iy >= 0 && iy < a.H && ix >= 0 && ix < a.W
+                             ? __ldg(reinterpret_cast<const int4*>(a.img + ((size_t(cb) * a.H + iy) * a.W + ix) * 4)) : make_int4(0, 0, 0, 0);
+                    }
                 } else {
                     const int k = (kb0 + i) * Cfg::BK + half * 32;
                     const int32_t* src = nullptr;
@@ -266,7 +283,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
         const int q = warp & 3, hq = ew >> 2;            // TMEM lane quarter (fixed by warp % 4), column slice
         const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
         const int2* lut = (Cfg::SLUT && a.Lphi && lut_in_range) ? s_lut : nullptr;   // else the table in global memory
-        uint8_t* yb = (Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 : nullptr;
+        YBox yb{(Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 * Cfg::YB_N : nullptr, Cfg::YB_N, 0};
         bool ok = true;
         int tl = 0;
         // Every epilogue warp runs every tile and every named barrier, also after a timed-out wait (it then skips
@@ -296,7 +313,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[b]);
         }
-        if (yb && lane == 0) bulk_wait0();        // every TMA store of Y has completed before the CTA exits
+        if (yb.base && lane == 0) bulk_wait0();   // every TMA store of Y has completed before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
