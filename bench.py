@@ -69,7 +69,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", choices=["attention", "gemm", "gn_conv", "linear", "geglu", "qkv", "norms"], default=None,
                     help="run only the named kernel(s) at the BASELINE config shape (attention: config 2, gemm: config 1, "
-                         "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 for 640 ch 32x32 / 1280 ch 16x16), "
+                         "gn_conv: config 3 at 320 ch 64x64, or --conv-level 1 / 2 / 3 for 640 ch 32x32 / 1280 ch 16x16 / 1280 ch 8x8), "
                          "linear: the UNet's int32-input linear with residual at 64x64 (M 32768, K --linear-k, N 320), "
                          "geglu: its planar GEGLU GEMM (M 32768, K 320, N 2560); qkv: the merged q|k|v GEMM with head "
                          "quantisation (M 32768, K 320, N 960); norms: GroupNorm statistics, "
@@ -77,7 +77,7 @@ def parse():
                          "print their CUDA-event times as one JSON line and exit; with --impl reference the reference's own "
                          "kernels at the same shapes")
     ap.add_argument("--linear-k", type=int, default=320)
-    ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2])
+    ap.add_argument("--conv-level", type=int, default=0, choices=[0, 1, 2, 3])
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -333,8 +333,10 @@ class GemmCase:
 
 class GnConvCase:
     """Config 3: GroupNorm (32 groups) + SiLU of int32 NHWC [8, H*W, C] (uniform over the int16 range), pixel max,
-    3x3 window exponents, then the implicit 3x3 conv C -> C with int8 weights."""
-    LEVELS = [(64, 320), (32, 640), (16, 1280)]
+    3x3 window exponents, then the implicit 3x3 conv C -> C with int8 weights, given the engine's 64 MiB split-K
+    workspace.  Levels 0-2 are the configuration's shapes; level 3 (1280 ch at 8x8, the UNet's deepest level) is the
+    shape where the conv splits K and runs the split-K reduction."""
+    LEVELS = [(64, 320), (32, 640), (16, 1280), (8, 1280)]
 
     def __init__(self, device, level):
         import ctypes
@@ -361,7 +363,9 @@ class GnConvCase:
         self.out = torch.empty((B, T, N), dtype=torch.int32, device=device)
         a = abi.ASrc(); a.src = abi.SRC_CONV32; a.img = self.Y.data_ptr(); a.H = Hh; a.W = Hh; a.C = C; a.stride = 1; a.Ho = Hh; a.Wo = Hh
         a.K = K; a.e = self.ce.data_ptr()
+        self.ws = torch.empty((64 << 20,), dtype=torch.uint8, device=device)
         E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = self.out.data_ptr(); E.ldy = N
+        E.workspace = self.ws.data_ptr(); E.workspace_bytes = 64 << 20
         self.a, self.E, self.dims = a, E, (B, Hh, C, T, N, K)
         self.stream = torch.cuda.current_stream(device)
         self.P = lambda x: ctypes.c_void_p(x.data_ptr())
@@ -384,7 +388,8 @@ class GnConvCase:
         self.gn(); self.conv()
 
     def report_norms(self):
-        """GroupNorm statistics, GroupNorm + SiLU apply (int32 + pixel max) and LayerNorm -> planes, timed apart"""
+        """GroupNorm statistics, GroupNorm + SiLU apply (int32 + pixel max), GroupNorm -> int8 planes (the transformer
+        blocks' input norm) and LayerNorm -> planes, timed apart"""
         import torch
         B, Hh, C, T, N, K = self.dims
         st, P = self.stream.cuda_stream, self.P
@@ -395,10 +400,14 @@ class GnConvCase:
         hi = torch.empty((B * T, C), dtype=torch.int8, device=self.X.device); lo = torch.empty_like(hi)
         e = torch.empty((B * T,), dtype=torch.int32, device=self.X.device)
         ln = lambda: self.V.check(self.L.vela_lnorm_q(st, P(self.X), B * T, C, P(self.gam), P(self.beta), 100000, P(hi), P(lo), P(e), C))
+        applyq = lambda: self.V.check(self.L.vela_gn_apply_row(st, P(self.X), B, T, C, 32, P(self.gs), P(self.gam), P(self.beta), None,
+                                                                None, None, P(hi), P(lo), P(e), C))
         ts, ta, tl = _time_ms(self.stream, stats), _time_ms(self.stream, apply), _time_ms(self.stream, ln)
+        tq = _time_ms(self.stream, applyq)
         nb = B * T * C * 4
         return {"kernel": "norms (320 ch 64x64)", "gn_stats_ms": round(ts, 4), "gn_stats_gbs": round(2 * nb / ts / 1e6, 1),
                 "gn_apply_ms": round(ta, 4), "gn_apply_gbs": round((2 * nb + B * T * 4) / ta / 1e6, 1),
+                "gn_apply_q_ms": round(tq, 4), "gn_apply_q_gbs": round((nb + nb // 2 + B * T * 4) / tq / 1e6, 1),
                 "lnorm_q_ms": round(tl, 4), "lnorm_q_gbs": round((nb + nb // 2) / tl / 1e6, 1)}
 
     def report(self):
@@ -477,15 +486,16 @@ class LinearCase:
         rep = {"kernel": f"gemm_w8a16 {self.kind} (64x64 level)", "M": M, "N": N, "K": K, "ms": round(ms, 4),
                "int8_tops": round(2 * 2 * M * N * K / ms / 1e9, 2)}
         if self.kind == "linear":
-            # the same product with the input quantised once into planes first (vela_quant_rows) and the planar GEMM
+            # the same product the way the engine runs it at these sizes: the input quantised once into planes with its
+            # row maxima already known (vela_quant_rows_rm), then the planar GEMM
             import torch
             from vela_b200 import abi
             hi = torch.empty((M, K), dtype=torch.int8, device=self.X.device); lo = torch.empty_like(hi)
             e = torch.empty((M,), dtype=torch.int32, device=self.X.device)
             a = abi.ASrc(); a.src = abi.SRC_I8; a.hi = hi.data_ptr(); a.lo = lo.data_ptr(); a.ld8 = K; a.e = e.data_ptr()
             st = self.stream.cuda_stream
-            quant = lambda: self.V.check(self.L.vela_quant_rows(st, self.ptr(self.X.data_ptr()), M, K, K, self.ptr(hi.data_ptr()),
-                                                                self.ptr(lo.data_ptr()), self.ptr(e.data_ptr()), K))
+            quant = lambda: self.V.check(self.L.vela_quant_rows_rm(st, self.ptr(self.X.data_ptr()), self.ptr(self.rm_in.data_ptr()), M, K, K,
+                                                                   self.ptr(hi.data_ptr()), self.ptr(lo.data_ptr()), self.ptr(e.data_ptr()), K, M))
             gemm = lambda: self.V.check(self.L.vela_gemm_w8a16(st, self.byref(a), M, M, self.ptr(self.W.data_ptr()), K, N, N, K,
                                                                self.ptr(self.cst.data_ptr()), self.byref(self.E)))
             quant()

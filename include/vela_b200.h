@@ -102,6 +102,10 @@ int vela_conv_e(void* stream, const uint32_t* pm, int B, int H, int W, int strid
 /* Per-row power-of-two quantisation of X[M, K] (row stride ldx) into hi/lo [*, Kp] + e[M]; columns
  * [K, Kp) and rows [M, align32(M)) are written as the value 0.  k_quant_rows (src/kernels.h:14). */
 int vela_quant_rows(void* stream, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp);
+/* vela_quant_rows with the row maxima already known (rowmax[r] = max_c |X[r, c]|, as the producing GEMM epilogues
+ * and norms write them): e[r] = the exponent of rowmax[r], rows [M, Mpad) written as the value 0; K % 4 == 0.
+ * No reference counterpart (the reference's engine re-reads each row for its maximum). */
+int vela_quant_rows_rm(void* stream, const int32_t* X, const uint32_t* rowmax, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp, int Mpad);
 /* pm[r] = max_c |X[r, c]|.  k_pixmax (src/kernels.h:19). */
 int vela_pixmax(void* stream, const int32_t* X, int rows, int C, uint32_t* pm);
 /* 3x3 pad-1 im2col with per-output-pixel quantisation, K index tap*C + c.  k_im2col3 (src/kernels.h:21-22). */

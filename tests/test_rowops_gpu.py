@@ -36,6 +36,19 @@ def test_quant_rows(golden):
         assert np.array_equal(H(hi), g[f"hi{mode}"]) and np.array_equal(H(lo), g[f"lo{mode}"]) and np.array_equal(H(e)[:M], g[f"e{mode}"])
 
 
+def test_quant_rows_with_known_maxima(golden):
+    """vela_quant_rows_rm (the engine's form: row maxima from the producer) equals vela_quant_rows on the golden rows,
+    padding rows [M, Mpad) included"""
+    g = golden("quant_rows"); d = Dev()
+    for mode in range(3):
+        X = g[f"X{mode}"]; M, K = X.shape; Kp, Mp = 336, 96
+        rm = np.zeros(Mp, np.uint32); rm[:M] = np.abs(X.astype(np.int64)).max(1)
+        hi, lo, e = d.empty((Mp, Kp), torch.int8, 0x5A), d.empty((Mp, Kp), torch.int8, 0x5A), d.empty((Mp,), torch.int32, 0x5A)
+        ok(lib().vela_quant_rows_rm(None, P(d(X)), P(d(rm.view(np.int32))), M, K, K, P(hi), P(lo), P(e), Kp, Mp))
+        assert np.array_equal(H(hi), g[f"hi{mode}"]) and np.array_equal(H(lo), g[f"lo{mode}"]) and np.array_equal(H(e)[:M], g[f"e{mode}"])
+        assert (H(e)[M:] == 0).all()
+
+
 def test_im2col_pixmax_conv_e(golden):
     g = golden("im2col"); d = Dev()
     i = 0

@@ -44,6 +44,7 @@ SIGNATURES = {
     "vela_gemm_hl": (I, [P, P, P, I, I, I, P, I, I, I, I, P, P, P, I, P, I, I, P, P, P]),
     "vela_conv_e": (I, [P, P, I, I, I, I, P]),
     "vela_quant_rows": (I, [P, P, I, I, I, P, P, P, I]),
+    "vela_quant_rows_rm": (I, [P, P, P, I, I, I, P, P, P, I, I]),
     "vela_pixmax": (I, [P, P, I, I, P]),
     "vela_im2col3": (I, [P, P, P, I, I, I, I, I, P, P, P, I]),
     "vela_gn_stats": (I, [P, P, I, I, I, I, LL, P]),

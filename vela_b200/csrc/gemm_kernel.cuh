@@ -47,17 +47,29 @@ struct GemmArgs {
 
 __device__ __forceinline__ int ws128(int4 c) { return 128 * c.w; }
 
-// An epilogue warp's shared-memory boxes for the TMA stores of Y: n (1 or 2) boxes of 2 KB from base, used in turn;
-// i counts the stores issued so far (null base: no TMA stores).
+// An epilogue warp's shared-memory boxes (2 KB each) for the TMA stores of Y.  One box: a plain pointer, each store
+// waits until the previous one has read the box.  Several boxes (YBox, by reference): n boxes used in turn, i counts
+// the warp's stores, and with two boxes a store waits only for the one before the previous.  A null base means no
+// TMA stores.
 struct YBox { uint8_t* base; int n; int i; };
+__device__ __forceinline__ bool ybox_on(const uint8_t* p) { return p != nullptr; }
+__device__ __forceinline__ bool ybox_on(const YBox& b) { return b.base != nullptr; }
+__device__ __forceinline__ uint8_t* ybox_cur(uint8_t* p) { return p; }
+__device__ __forceinline__ uint8_t* ybox_cur(const YBox& b) { return b.base + (b.i & (b.n - 1)) * 2048; }
+__device__ __forceinline__ void ybox_wait(const uint8_t*) { bulk_wait_read0(); }
+__device__ __forceinline__ void ybox_wait(const YBox& b) { if (b.n == 2) bulk_wait_read1(); else bulk_wait_read0(); }
+__device__ __forceinline__ void ybox_next(uint8_t*) {}
+__device__ __forceinline__ void ybox_next(YBox& b) { ++b.i; }
+
 
 // Epilogue of one 128 x BN tile for one thread = one output row (rl) and the NC columns [c0, c0 + NC) of the tile
 // (q|k|v: NC = 64, one head): reads the hi / lo accumulators from TMEM (tl = the thread's lane-quarter base),
 // applies the per-column constants (cst[j] = column n0 + j) and writes the epilogue's outputs.  er is the row's
-// exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory).
-template <int BN, int SRC, int EPI, int NC, bool FAST>
+// exponent; L2 the GELU table staged in shared memory (null: read a.Lphi from global memory); yb the warp's boxes for
+// the TMA stores of a plain epilogue (uint8_t* or YBox2&, see above).
+template <int BN, int SRC, int EPI, int NC, bool FAST, class YB>
 __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                int m0, int n0, int rl, int c0, int split, int er, YBox& yb) {
+                                                int m0, int n0, int rl, int c0, int split, int er, YB yb) {
     static_assert(NC % 16 == 0, "16-column chunks");
     const int grow = m0 + rl;
     const bool live = grow < a.Mreal;
@@ -136,7 +148,7 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             int hi[16], lo[16];
             tmem_ld16(tl + col, hi); tmem_ld16(tl + BN + col, lo); tmem_ld_wait();
             // a TMA-stored plain chunk is written by the whole warp (rows past Mreal are clipped by the store)
-            const bool tstore = EPI == EPI_PLAIN && yb.base != nullptr;
+            const bool tstore = EPI == EPI_PLAIN && ybox_on(yb);
             if (!act && !tstore) continue;
             if (a.partial) {             // split-K: raw accumulators, reduced by gemm_splitk_reduce
                 int32_t* ph = a.partial + (size_t(split) * 2 * a.Mp + grow) * a.Np + n;
@@ -151,9 +163,9 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
             if constexpr (EPI == EPI_PLAIN) {
                 // four columns at a time: y, GELU, + residual, then out (shared-memory box or global) and the row max
                 const int lane = rl & 31;
-                uint8_t* box = yb.base + (yb.i & (yb.n - 1)) * 2048;
+                uint8_t* box = ybox_cur(yb);
                 if (tstore) {                            // the store that last used this box has finished reading it
-                    if (lane == 0) { if (yb.n == 2) bulk_wait_read1(); else bulk_wait_read0(); }
+                    if (lane == 0) ybox_wait(yb);
                     __syncwarp();
                 }
                 const int32_t* rp = a.R + size_t(grow) * a.ldy + n;
@@ -197,7 +209,7 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) { tma_store_2d(&a.tmY, box, n, m0 + (rl & ~31)); bulk_commit(); }
-                    ++yb.i;
+                    ybox_next(yb);
                 }
             } else {
                 int y[16];
@@ -236,16 +248,16 @@ __device__ __forceinline__ void gemm_epilogue_t(const GemmArgs& a, uint32_t tl, 
 // decision is warp-uniform (srange = the tile's min and max s; the caller votes).
 // (the general arithmetic stays out of line: it is rare and would otherwise raise the register count of the
 // common path)
-template <int BN, int SRC, int EPI, int NC>
+template <int BN, int SRC, int EPI, int NC, class YB>
 __device__ __noinline__ void gemm_epilogue_general(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                                   int m0, int n0, int rl, int c0, int split, int er, YBox& yb) {
-    gemm_epilogue_t<BN, SRC, EPI, NC, false>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
+                                                   int m0, int n0, int rl, int c0, int split, int er, YB yb) {
+    gemm_epilogue_t<BN, SRC, EPI, NC, false, YB>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }
-template <int BN, int SRC, int EPI, int NC>
+template <int BN, int SRC, int EPI, int NC, class YB>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t tl, const int4* __restrict__ cst, const int2* __restrict__ L2,
-                                              int m0, int n0, int rl, int c0, int split, int er, bool fast, YBox& yb) {
-    if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
-    else gemm_epilogue_general<BN, SRC, EPI, NC>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
+                                              int m0, int n0, int rl, int c0, int split, int er, bool fast, YB yb) {
+    if (fast) gemm_epilogue_t<BN, SRC, EPI, NC, true, YB>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
+    else gemm_epilogue_general<BN, SRC, EPI, NC, YB>(a, tl, cst, L2, m0, n0, rl, c0, split, er, yb);
 }
 
 // Split-K reduction: sum the raw hi/lo partials of every split, then the plain epilogue

@@ -35,25 +35,31 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     // epilogue warps: 16 (four per TMEM lane quarter) for planar sources, 8 where converters share the SM or a
     // q|k|v head (64 columns) is one thread's unit
     static constexpr int EW = (REG || EPI == EPI_QKV) ? 8 : 16;
-    static constexpr int NCOL = BN / (EW / 4);                 // columns of a tile per epilogue thread
+    // with two accumulator buffers and 16 epilogue warps, two groups of 8 take alternate tiles (group g drains
+    // buffer g), so the latency chains of two tiles' epilogues (constants, residual, TMEM loads, stores) overlap
+    // (the GEGLU and split epilogues; the plain one measured faster with all 16 warps on every tile)
+    static constexpr int EG = (EW == 16 && ACC_BUFS == 2 && EPI != EPI_PLAIN) ? 2 : 1;
+    static constexpr int EWG = EW / EG;                         // epilogue warps per group
+    static constexpr int NCOL = BN / (EWG / 4);                // columns of a tile per epilogue thread
     static constexpr int EPI_WARP0 = 2 + NCW;
     static constexpr int XW = REG ? 1 : 0;                      // int32 sources: one more warp issues the staging TMA
     static constexpr int X_WARP = EPI_WARP0 + EW;
     static constexpr int THREADS = 32 * (2 + NCW + EW + XW);
     static constexpr int CTRL = 1024;
     static constexpr bool SLUT = !REG;                          // GELU table staged in shared memory
-    static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [2][BN] column constants (double-buffered by tile)
-    static constexpr int OFF_LUT = OFF_CST + 2 * BN * 16;       // int2[LUT_S_ENTRIES]
-    // plain epilogue: 32 x 16 int32 boxes (2 KB, 64-byte swizzle) per epilogue warp for the TMA stores of Y.  The
-    // wide int32-source tiles (several 16-column chunks per thread) take two boxes per warp, one filled while the
-    // other's store drains, where they fit without costing the staging ring a stage; the planar tiles (one chunk
-    // per thread and tile) keep one, which measured faster there.
+    static constexpr int OFF_CST = STAGES * STAGE + CTRL;       // [EG][2][BN] column constants (per group, double-buffered)
+    static constexpr int OFF_LUT = OFF_CST + EG * 2 * BN * 16;  // int2[LUT_S_ENTRIES]
+    // plain epilogue: 32 x 16 int32 boxes (2 KB, 64-byte swizzle) per epilogue warp for the TMA stores of Y.  A
+    // thread with several 16-column chunks per tile takes two boxes per warp, one filled while the other's store
+    // drains, where they fit (for int32 sources: without costing the staging ring a stage); one chunk, one box.
     static constexpr int YB_ONE = EPI == EPI_PLAIN ? EW * 2048 : 0;
     static constexpr int OFF_YB = (OFF_LUT + (SLUT ? LUT_S_ENTRIES * 8 : 0) + 1023) / 1024 * 1024;
     static constexpr int X_HALF = BM * 128, X_STAGE = 2 * X_HALF;
     static constexpr int XF1 = REG ? (227 * 1024 - 1024 - OFF_YB - YB_ONE) / X_STAGE : 0;
     static constexpr int XF2 = REG ? (227 * 1024 - 1024 - OFF_YB - 2 * YB_ONE) / X_STAGE : 0;
-    static constexpr int YB_N = EPI == EPI_PLAIN && REG && (XF2 < 4 ? XF2 : 4) >= (XF1 < 4 ? XF1 : 4) ? 2 : 1;
+    static constexpr int YB_N = EPI != EPI_PLAIN || NCOL < 32 ? 1
+                              : REG ? ((XF2 < 4 ? XF2 : 4) >= (XF1 < 4 ? XF1 : 4) ? 2 : 1)
+                                    : (1024 + OFF_YB + 2 * YB_ONE <= 227 * 1024 ? 2 : 1);
     static constexpr int YB_BYTES = YB_N * YB_ONE;
     static constexpr int OFF_X = OFF_YB + YB_BYTES;
     static constexpr int X_FIT = REG ? (227 * 1024 - 1024 - OFF_X) / X_STAGE : 0;
@@ -92,7 +98,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1 + Cfg::NCW); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], Cfg::EW); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], Cfg::EWG); }
         for (int s = 0; s < 4; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], Cfg::NCW > 0 ? Cfg::NCW : 1); }
         mbar_fence_init();
     }
@@ -279,25 +285,27 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
     } else if (warp < Cfg::EPI_WARP0 + Cfg::EW) {
         // ------------------------------------------------------------ epilogue
         const int ew = warp - Cfg::EPI_WARP0;            // 0 .. EW-1
-        const int et = threadIdx.x - Cfg::EPI_WARP0 * 32;
-        const int q = warp & 3, hq = ew >> 2;            // TMEM lane quarter (fixed by warp % 4), column slice
+        const int grp = Cfg::EG == 1 ? 0 : ew / Cfg::EWG, ewg = ew - grp * Cfg::EWG;   // group (tile parity when EG = 2), warp in it
+        const int et = ewg * 32 + lane;
+        const int q = warp & 3, hq = ewg >> 2;           // TMEM lane quarter (fixed by warp % 4), column slice
         const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
         const int2* lut = (Cfg::SLUT && a.Lphi && lut_in_range) ? s_lut : nullptr;   // else the table in global memory
-        YBox yb{(Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 * Cfg::YB_N : nullptr, Cfg::YB_N, 0};
+        uint8_t* yb = (Cfg::YB_BYTES > 0 && a.ytma) ? smem + Cfg::OFF_YB + ew * 2048 * Cfg::YB_N : nullptr;
+        YBox yb2{yb, Cfg::YB_N, 0};
         bool ok = true;
-        int tl = 0;
-        // Every epilogue warp runs every tile and every named barrier, also after a timed-out wait (it then skips
-        // the work), so no warp waits on a barrier that another one has left.
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+        // Every epilogue warp runs every tile of its group and every named barrier, also after a timed-out wait (it
+        // then skips the work), so no warp waits on a barrier that another one has left.
+        for (int t = blockIdx.x + grp * gridDim.x, tl = grp; t < ntiles; t += Cfg::EG * gridDim.x, tl += Cfg::EG) {
             const int b = Cfg::ACC_BUFS == 2 ? (tl & 1) : 0, u = Cfg::ACC_BUFS == 2 ? (tl >> 1) : tl;
             const int z = t / nMN, r = t - z * nMN, m0 = (r / nN) * Cfg::BM, n0 = (r % nN) * BN;
             // this tile's column constants and the row exponent, fetched while the MMAs run
-            int4* cb = s_cst + (tl & 1) * BN;
-            for (int i = et; i < BN; i += Cfg::EW * 32) cb[i] = n0 + i < a.Np ? __ldg(a.cst + n0 + i) : make_int4(1, 0, 0, 0);
+            int4* cb = s_cst + (Cfg::EG == 1 ? (tl & 1) : grp * 2 + ((tl >> 1) & 1)) * BN;
+            for (int i = et; i < BN; i += Cfg::EWG * 32) cb[i] = n0 + i < a.Np ? __ldg(a.cst + n0 + i) : make_int4(1, 0, 0, 0);
             const int grow = m0 + q * 32 + lane;
             int er = 0;
             if (grow < a.Mreal) er = (SRC == SRC_X32) ? row_exp(__ldg(a.rowmax_in + grow)) : __ldg(a.e + grow);
-            asm volatile("bar.sync 2, %0;" :: "r"(Cfg::EW * 32) : "memory");
+            if (Cfg::EG == 1) asm volatile("bar.sync 2, %0;" :: "r"(Cfg::EWG * 32) : "memory");
+            else asm volatile("bar.sync %0, %1;" :: "r"(2 + grp), "r"(Cfg::EWG * 32) : "memory");
             // the tile's range of column shifts s (each lane scans a slice of the staged constants)
             // and of |m| (the short arithmetic forms 256 m in 32 bits)
             int smin = INT_MAX, smax = INT_MIN;
@@ -308,12 +316,13 @@ __global__ void __launch_bounds__(PersistCfg<BN, STAGES, SRC, EPI>::THREADS, 1) 
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], u & 1, a.err, DEVERR_TIMEOUT_ACC, a.wait_limit));
             if (!ok) continue;
             tc_fence_after();
-            gemm_epilogue<BN, SRC, EPI, Cfg::NCOL>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast, yb);
+            if constexpr (Cfg::YB_N == 2) gemm_epilogue<BN, SRC, EPI, Cfg::NCOL, YBox&>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast, yb2);
+            else gemm_epilogue<BN, SRC, EPI, Cfg::NCOL, uint8_t*>(a, tq + uint32_t(b * Cfg::ACC_COLS), cb, lut, m0, n0, q * 32 + lane, hq * Cfg::NCOL, z, er, fast, yb);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[b]);
         }
-        if (yb.base && lane == 0) bulk_wait0();   // every TMA store of Y has completed before the CTA exits
+        if (yb && lane == 0) bulk_wait0();        // every TMA store of Y has completed before the CTA exits
     }
     tc_fence_before();
     __syncthreads();

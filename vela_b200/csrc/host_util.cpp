@@ -67,6 +67,23 @@ int sm_count() {
     return n;
 }
 
+int blocks_per_sm(const void* kernel, int threads, size_t smem) {
+    struct Entry { int dev; const void* k; int threads; size_t smem; int blocks; };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    const int d = current_device();
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        for (const Entry& e : cache) if (e.dev == d && e.k == kernel && e.threads == threads && e.smem == smem) return e.blocks;
+    }
+    int n = 0;
+    VELA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem));
+    n = n > 0 ? n : 1;
+    std::lock_guard<std::mutex> lk(mu);
+    cache.push_back(Entry{d, kernel, threads, smem, n});
+    return n;
+}
+
 void register_error_word(const void* symbol) {
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto* s : g_symbols) if (s == symbol) return;

@@ -30,6 +30,9 @@ void register_error_word(const void* symbol);
 
 int current_device();
 int sm_count();
+// Blocks of `kernel` resident on one SM at `threads` threads and `smem` dynamic shared bytes (at least 1), on the
+// current device; cached.  Grids of this many blocks per SM run in one wave.
+int blocks_per_sm(const void* kernel, int threads, size_t smem);
 
 // Per-launch options of the kernels with bounded waits (GEMM, attention).
 struct LaunchOpts {

@@ -680,7 +680,10 @@ void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H
 void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs) {
     VELA_REQUIRE(X && gs && B > 0 && T > 0 && C % 32 == 0 && C <= 4096, "gn_stats: C must be a multiple of 32 (32 groups), at most 4096");
     const int cnt = B * 32, Q = C / 4, RP = std::max(1, 512 / Q);
-    const int chunks = std::max(1, std::min(ceil_div(T, 4 * RP), (sm_count() * 4) / B));
+    // one wave: as many blocks as stay resident (pass 2, the larger register footprint, decides), each a long run
+    // of rows, so no second wave waits on the first and every block's prologue and reduction are paid once per SM
+    const int resident = sm_count() * blocks_per_sm(reinterpret_cast<const void*>(gn_stats_kernel<2>), Q * RP, 0);
+    const int chunks = std::max(1, std::min(ceil_div(T, 4 * RP), resident / B));
     const int rpb = ceil_div(T, chunks);
     gn_init_kernel<<<ceil_div(cnt, 256), 256, 0, st>>>(gs, cnt);
     const dim3 grid(ceil_div(T, rpb), B);
@@ -697,12 +700,15 @@ void gn_apply(cudaStream_t st, const int32_t* X, int B, int T, int C, const vela
     if (hi) rpb = std::min(rpb, std::max(1, 24576 / (4 * C)));
     if (rpb > 2 * T) rpb = std::max(1, 2 * T);
     const int rp = std::min(RP, rpb);
-    const unsigned blocks = std::min(ceil_div(M, rpb), sm_count() * 4);
+    // the blocks walk the row chunks: one wave of resident blocks
     if (hi) {
         VELA_REQUIRE(lo && e && Kp >= C && Kp % 4 == 0 && C <= 6144, "gn_apply: quantised output needs lo, e, C <= 6144 and Kp >= C, Kp % 4 == 0");
-        gn_apply_kernel<true><<<blocks, PT * rp, size_t(rpb) * C * 4, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
+        const size_t sm = size_t(rpb) * C * 4;
+        const unsigned blocks = std::min(ceil_div(M, rpb), sm_count() * blocks_per_sm(reinterpret_cast<const void*>(gn_apply_kernel<true>), PT * rp, sm));
+        gn_apply_kernel<true><<<blocks, PT * rp, sm, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
     } else {
         VELA_REQUIRE(Y && pm, "gn_apply: int32 output needs Y and pm");
+        const unsigned blocks = std::min(ceil_div(M, rpb), sm_count() * blocks_per_sm(reinterpret_cast<const void*>(gn_apply_kernel<false>), PT * rp, 0));
         gn_apply_kernel<false><<<blocks, PT * rp, 0, st>>>(X, M, T, C, gs, g, beta, Lsig, Y, pm, hi, lo, e, Kp, rpb);
     }
 }
@@ -777,6 +783,10 @@ using namespace vela;
 
 extern "C" int vela_quant_rows(void* stream, const int32_t* X, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
     return guarded("vela_quant_rows", [&] { quant_rows(ST, X, M, K, ldx, hi, lo, e, Kp); });
+}
+extern "C" int vela_quant_rows_rm(void* stream, const int32_t* X, const uint32_t* rowmax, int M, int K, int ldx, int8_t* hi, int8_t* lo, int32_t* e,
+                                  int Kp, int Mpad) {
+    return guarded("vela_quant_rows_rm", [&] { quant_rows_rm(ST, X, rowmax, M, K, ldx, hi, lo, e, Kp, Mpad); });
 }
 extern "C" int vela_pixmax(void* stream, const int32_t* X, int rows, int C, uint32_t* pm) {
     return guarded("vela_pixmax", [&] { pixmax(ST, X, rows, C, pm); });
