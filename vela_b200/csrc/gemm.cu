@@ -48,19 +48,19 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
 VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_SPLIT3) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_QKV)
 #define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 4, SRC, EPI_PLAIN) \
-    VELA_PERSIST_EXTERN(160, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(224, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 4, SRC, EPI_PLAIN)
+    VELA_PERSIST_EXTERN(160, 4, SRC, EPI_PLAIN)
 VELA_PERSIST_REG(SRC_X32) VELA_PERSIST_REG(SRC_CONV32)
 
 namespace {
-constexpr int REG_BNS[5] = {64, 128, 160, 224, 256};
+// int32 sources: up to 160 columns (two 160-wide hi | lo accumulators fill the tensor memory; wider tiles measured
+// slower on the UNet's convs, their one accumulator buffer leaving the MMAs idle for a longer epilogue)
+constexpr int REG_BNS[3] = {64, 128, 160};
 
 template <int SRC> void dispatch_reg(int BN, const GemmArgs& a, cudaStream_t st) {
     switch (BN) {
         case 64: launch_gemm_persist<64, 4, SRC, EPI_PLAIN>(a, st); break;
         case 128: launch_gemm_persist<128, 4, SRC, EPI_PLAIN>(a, st); break;
-        case 160: launch_gemm_persist<160, 4, SRC, EPI_PLAIN>(a, st); break;
-        case 224: launch_gemm_persist<224, 4, SRC, EPI_PLAIN>(a, st); break;
-        default: launch_gemm_persist<256, 4, SRC, EPI_PLAIN>(a, st); break;
+        default: launch_gemm_persist<160, 4, SRC, EPI_PLAIN>(a, st); break;
     }
 }
 
@@ -77,7 +77,7 @@ Plan plan(int src, int epi, int Mp, int Mreal, int Np, int Nreal, int nkb, size_
     const int nM = ceil_div(Mp, 128);
     Plan best{reg ? 128 : 64, 1};
     double best_t = 1e30;
-    const int nb = reg ? 5 : 2;
+    const int nb = reg ? 3 : 2;
     const int i8_bns[2] = {64, 128};
     for (int i = 0; i < nb; ++i) {
         const int bn = reg ? REG_BNS[i] : i8_bns[i];

@@ -4,6 +4,4 @@ namespace vela {
 template void launch_gemm_persist<64, 4, SRC_X32, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
 template void launch_gemm_persist<128, 4, SRC_X32, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
 template void launch_gemm_persist<160, 4, SRC_X32, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
-template void launch_gemm_persist<224, 4, SRC_X32, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
-template void launch_gemm_persist<256, 4, SRC_X32, EPI_PLAIN>(const GemmArgs&, cudaStream_t);
 }  // namespace vela
