@@ -67,9 +67,9 @@ constexpr int KAUX_BYTES = KAUX_QI + 4 * 4;
 constexpr int QI_MODE = 8, QI_FULL = 1 << 10;
 // P.V accumulator columns in TMEM
 constexpr uint32_t PV_A = 192, PV_Y = PV_A + PV_N, PV_D = PV_Y + PV_N;
-constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025] exp table (see exp_fast / exp_general); entry 1024 = (0, 0)
+constexpr int OFF_LUT = OFF_KAUX + KS * KAUX_BYTES;    // int2[1025] exp table (see exp_fast_d / exp_general); entry 1024 = (0, 0)
 constexpr int SW = 16;                                 // softmax warps: four per TMEM lane quarter, 16 keys each
-constexpr int AUX_WARP = 2 + SW;                      // per K stage: kc and the quarters' exponent range, once per CTA
+constexpr int AUX_WARP = 2 + SW;                      // per K stage: kc and the quarters' info words, once per CTA
 constexpr int THREADS = 32 * (3 + SW);
 constexpr int OFF_RED = OFF_LUT + 1032 * 8;            // cross-warp reductions: 4 x 128 x 8 bytes
 constexpr int OFF_BAR = OFF_RED + 4 * 128 * 8;
