@@ -333,9 +333,11 @@ class GemmCase:
 
 class GnConvCase:
     """Config 3: GroupNorm (32 groups) + SiLU of int32 NHWC [8, H*W, C] (uniform over the int16 range), pixel max,
-    3x3 window exponents, then the implicit 3x3 conv C -> C with int8 weights, given the engine's 64 MiB split-K
-    workspace.  Levels 0-2 are the configuration's shapes; level 3 (1280 ch at 8x8, the UNet's deepest level) is the
-    shape where the conv splits K and runs the split-K reduction."""
+    then the 3x3 conv C -> C with int8 weights the way the engine runs it, given the engine's 64 MiB split-K
+    workspace: at 320 / 640 channels the implicit conv (3x3 window exponents, windows quantised on load); at 1280
+    channels (16x16 and 8x8) the explicit im2col into hi / lo planes (window exponents included) and the planar GEMM.
+    Levels 0-2 are the configuration's shapes; level 3 (1280 ch at 8x8, the UNet's deepest level) is the shape where
+    the GEMM splits K and runs the split-K reduction.  The implicit form is also timed at every level."""
     LEVELS = [(64, 320), (32, 640), (16, 1280), (8, 1280)]
 
     def __init__(self, device, level):
@@ -367,6 +369,15 @@ class GnConvCase:
         E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = self.out.data_ptr(); E.ldy = N
         E.workspace = self.ws.data_ptr(); E.workspace_bytes = 64 << 20
         self.a, self.E, self.dims = a, E, (B, Hh, C, T, N, K)
+        # the engine's rule (explicit_im2col in engine.cu): 1280 output channels on at most 16 x 16 pixels
+        self.explicit = N >= 1280 and T <= 256
+        if self.explicit:
+            Mp = (B * T + 63) // 64 * 64
+            self.hi = torch.empty((Mp, K), dtype=torch.int8, device=device); self.lo = torch.empty_like(self.hi)
+            self.pe = torch.empty((Mp,), dtype=torch.int32, device=device)
+            ap = abi.ASrc(); ap.src = abi.SRC_I8; ap.hi = self.hi.data_ptr(); ap.lo = self.lo.data_ptr(); ap.ld8 = K
+            ap.e = self.pe.data_ptr(); ap.K = K
+            self.ap, self.Mp = ap, Mp
         self.stream = torch.cuda.current_stream(device)
         self.P = lambda x: ctypes.c_void_p(x.data_ptr())
         self.byref = ctypes.byref
@@ -378,11 +389,19 @@ class GnConvCase:
         self.V.check(self.L.vela_gn_apply_row(st, P(self.X), B, T, C, 32, P(self.gs), P(self.gam), P(self.beta), P(self.Lsig),
                                               P(self.Y), P(self.pm), None, None, None, 0))
 
-    def conv(self):
+    def conv_implicit(self):
         B, Hh, C, T, N, K = self.dims
         st, P = self.stream.cuda_stream, self.P
         self.V.check(self.L.vela_conv_e(st, P(self.pm), B, Hh, Hh, 1, P(self.ce)))
         self.V.check(self.L.vela_gemm_w8a16(st, self.byref(self.a), B * T, B * T, P(self.W), K, N, N, K, P(self.cst), self.byref(self.E)))
+
+    def conv(self):
+        if not self.explicit:
+            return self.conv_implicit()
+        B, Hh, C, T, N, K = self.dims
+        st, P = self.stream.cuda_stream, self.P
+        self.V.check(self.L.vela_im2col3(st, P(self.Y), P(self.pm), B, Hh, Hh, C, 1, P(self.hi), P(self.lo), P(self.pe), K))
+        self.V.check(self.L.vela_gemm_w8a16(st, self.byref(self.ap), self.Mp, B * T, P(self.W), K, N, N, K, P(self.cst), self.byref(self.E)))
 
     def launch(self):
         self.gn(); self.conv()
@@ -413,11 +432,12 @@ class GnConvCase:
     def report(self):
         B, Hh, C, T, N, K = self.dims
         self.gn()
-        gms, cms = _time_ms(self.stream, self.gn), _time_ms(self.stream, self.conv)
+        gms, cms, ims = _time_ms(self.stream, self.gn), _time_ms(self.stream, self.conv), _time_ms(self.stream, self.conv_implicit)
         ops = 2 * 2 * B * T * N * K
-        return {"kernel": "GroupNorm+SiLU -> implicit 3x3 conv (config 3)", "B": B, "HW": Hh, "C": C,
+        return {"kernel": "GroupNorm+SiLU -> 3x3 conv (config 3)", "B": B, "HW": Hh, "C": C,
                 "gn_ms": round(gms, 4), "gn_gbs": round(B * T * C * 8 / gms / 1e6, 1),
-                "conv_ms": round(cms, 4), "conv_int8_tops": round(ops / cms / 1e9, 2)}
+                "conv_path": "explicit im2col + planar GEMM" if self.explicit else "implicit",
+                "conv_ms": round(cms, 4), "conv_int8_tops": round(ops / cms / 1e9, 2), "implicit_conv_ms": round(ims, 4)}
 
 
 class LinearCase:

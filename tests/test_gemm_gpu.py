@@ -144,6 +144,40 @@ def test_conv_320ch_16x16():
         assert np.array_equal(got, exp), stride
 
 
+@pytest.mark.parametrize("B,Hh,C,N,stride,Kp", [(8, 16, 256, 1280, 1, 2304), (4, 16, 128, 1280, 2, 1216)])
+def test_conv_explicit_im2col_deep(B, Hh, C, N, stride, Kp):
+    """the engine's deep-level convolution (1280 output channels at 16x16 and below): the window-quantised im2col
+    planes (one warp per row and tap) against the oracle's im2col; then the planar GEMM at deep K (36 / 19 k-blocks,
+    where the planner weighs 256-column tiles) -- the first 128 rows against the oracle's GEMM, every row against the
+    implicit conv of the same image"""
+    rng = np.random.default_rng(7 + stride); d = Dev()
+    X = rbits(rng, (B, Hh, Hh, C), 22)
+    Ho = (Hh - 1) // stride + 1; rows = B * Ho * Ho; Mp = (rows + 63) // 64 * 64
+    W = np.zeros((N, Kp), np.int8); W[:, :9 * C] = rng.integers(-127, 128, (N, 9 * C)).astype(np.int8)
+    c = cst_for(rng, W, N, N)
+    pm = O.pixmax(X, B * Hh * Hh, C)
+    dX, dpm, dW, dc = d(X), d(pm.view(np.int32)), d(W), d(c)
+    hi, lo, e = d.empty((Mp, Kp), torch.int8, 0x5A), d.empty((Mp, Kp), torch.int8, 0x5A), d.empty((Mp,), torch.int32, 0x5A)
+    V.check(V.lib().vela_im2col3(None, P(dX), P(dpm), B, Hh, Hh, C, stride, P(hi), P(lo), P(e), Kp))
+    ohi, olo, oe = O.im2col3(X, pm, B, Hh, Hh, C, stride, Kp, rows)
+    assert np.array_equal(H(hi)[:rows], ohi) and np.array_equal(H(lo)[:rows], olo) and np.array_equal(H(e)[:rows], oe)
+    Y = d.empty((rows, N), torch.int32, 0x5A)
+    E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = A(Y); E.ldy = N
+    run_gemm(planar_src(hi, lo, Kp, e), Mp, rows, dW, Kp, N, N, Kp, dc, E)
+    exp = np.zeros((128, N), np.int32)
+    O.gemm_hl(ohi[:128], olo[:128], 128, W, N, Kp, c, oe[:128], O.EPI_PLAIN, Y=exp, ldy=N)
+    got = H(Y)
+    assert np.array_equal(got[:128], exp)
+    ce = d.zeros(Mp, torch.int32)
+    V.check(V.lib().vela_conv_e(None, P(dpm), B, Hh, Hh, stride, P(ce)))
+    a = abi.ASrc(); a.src = abi.SRC_CONV32; a.img = A(dX); a.H = Hh; a.W = Hh; a.C = C; a.stride = stride; a.Ho = Ho; a.Wo = Ho
+    a.K = 9 * C; a.e = A(ce)
+    Yi = d.empty((rows, N), torch.int32, 0x5A)
+    Ei = abi.AEpi(); Ei.epi = abi.EPI_PLAIN; Ei.Y = A(Yi); Ei.ldy = N
+    run_gemm(a, Mp, rows, dW, Kp, N, N, Kp, dc, Ei)
+    assert np.array_equal(got, H(Yi))
+
+
 @pytest.mark.parametrize("B,Hh,N", [(2, 64, 320), (3, 10, 64)])
 def test_conv_4ch_input(B, Hh, N):
     """the UNet's input conv (4 channels, K = 36 padded to 48): nine 16-byte pixels per row quantised on load, no im2col

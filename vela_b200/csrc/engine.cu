@@ -7,8 +7,9 @@
 // the loader which weights are 3x3 kernels and which blocks are transformers.  The text encoder / setPrompt follow
 // src/engine.cu:491-574, the step and its pipeline :599-677 (forwardIO, graph per slot, submit / collect / run).
 // Differences by design:
-//   - every GEMM, convolution (implicit 3x3, any depth) and attention runs on the tcgen05 kernels;
-//     no cuBLASLt, no im2col buffer, no score buffers;
+//   - every GEMM, convolution and attention runs on the tcgen05 kernels; no cuBLASLt, no score buffers;
+//     3x3 convolutions quantise their windows while loading them (implicit GEMM), except the 1280-channel ones at
+//     16x16 and below, which quantise each window once into an im2col buffer for the planar GEMM;
 //   - weights are prepared once at load: 3x3 kernels permuted to tap-major K, N padded to 64,
 //     K to 16, q|k|v and the GEGLU a|g rows merged (a|g interleaved) exactly as the reference does;
 //   - the text encoder computes only the 77 real rows (every op on that path is row-local and the
@@ -613,6 +614,10 @@ private:
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_X32; A.x = xd; A.ldx = K; A.rowmax = rm; A.K = L.K;
         gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
     }
+    // Which 3x3 convolutions run as explicit im2col + planar GEMM: 1280 output channels on at most 16 x 16 pixels.
+    // Measured at batch 8 (explicit vs implicit): 0.097 vs 0.124 ms at 16x16, 0.046 vs 0.060 ms at 8x8; at 32x32
+    // with 640 channels the two tie and at 64x64 the 189 MB of planes would not stay in L2.
+    static bool explicit_im2col(const Lin& L, int out_pixels) { return L.N >= 1280 && out_pixels <= 256; }
     // 3x3 pad-1 convolution (Engine::conv3, src/engine.cu:254-280): implicit GEMM on the int32 image
     Tensor conv3(const Tensor& x, int H, int W, const Lin& L, int stride, int32_t* out = nullptr, const int32_t* residual = nullptr, const uint32_t* pmIn = nullptr) {
         VELA_REQUIRE(L.conv3 && x.C * 9 == L.K, "conv3: shape mismatch");
@@ -621,9 +626,20 @@ private:
         const size_t mk = arena_.off;
         const uint32_t* pm = pmIn;
         if (!pm) { uint32_t* p = static_cast<uint32_t*>(arena_.alloc(size_t(x.B) * H * W * 4)); pixmax(st_, x.d, x.B * H * W, x.C, p); pm = p; }
-        // every depth, the 4-channel input image included, is quantised while loaded: no im2col buffer
         const int Mp = int(align_up(rows, 64));
         int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
+        if (explicit_im2col(L, Ho * Wo) && x.C % 4 == 0) {
+            // the deep levels (1280 output channels at 16x16 and below): every window quantised once into hi / lo
+            // planes (the reference's engine takes its im2col path here too), then the planar GEMM with wide tiles;
+            // the implicit form would re-quantise each window for every one of its eight column tiles
+            int8_t* hi = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp)); int8_t* lo = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp));
+            im2col3(st_, x.d, pm, x.B, H, W, x.C, stride, hi, lo, e, L.Kp);
+            vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;
+            gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);
+            arena_.off = mk;
+            return y;
+        }
+        // the other depths, the 4-channel input image included, are quantised while loaded: no im2col buffer
         conv_e(st_, pm, x.B, H, W, stride, e);
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_CONV32; A.img = x.d; A.H = H; A.W = W; A.C = x.C; A.stride = stride; A.Ho = Ho; A.Wo = Wo; A.K = L.K; A.e = e;
         gemm_w8a16(st_, A, Mp, rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, epi_plain(y.d, L.N, residual, nullptr), lo_);

@@ -130,6 +130,45 @@ __global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restr
     pad_cols(h, l, K, Kp, lane);
 }
 
+// The same for C % 4 == 0 and Kp % 4 == 0: one warp per (output row, tap), four channels per lane and step (a
+// 16-byte load, four hi and four lo bytes stored as words); the row's window exponent from the nine pixel maxima
+// (a warp max), written by the tap-0 warp; the tap-8 warp also fills the K padding [9C, Kp).
+__global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __restrict__ pm, int B, int H, int W, int C, int stride, int Ho,
+                                  int Wo, int rows, int Mpad, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
+    const int lane = threadIdx.x & 31, wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int r = wg / 9, tap = wg - r * 9;
+    if (r >= Mpad) return;
+    u32* h = reinterpret_cast<u32*>(hi + size_t(r) * Kp);
+    u32* l = reinterpret_cast<u32*>(lo + size_t(r) * Kp);
+    const int q4 = C >> 2, k0 = tap * q4, kend = tap == 8 ? (Kp >> 2) : k0 + q4;
+    if (r >= rows) {
+        for (int c4 = k0 + lane; c4 < kend; c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
+        return;
+    }
+    const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
+    u32 m = 0;
+    if (lane < 9) {
+        const int iy = oy * stride - 1 + lane / 3, ix = ox * stride - 1 + lane % 3;
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W) m = __ldg(pm + (size_t(b) * H + iy) * W + ix);
+    }
+    const int ee = row_exp(__reduce_max_sync(0xffffffffu, m));
+    if (tap == 0 && lane == 0) e[r] = ee;
+    const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
+    const int iy = oy * stride - 1 + tap / 3, ix = ox * stride - 1 + tap % 3;
+    const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+    const int4* x = reinterpret_cast<const int4*>(X + ((size_t(b) * H + (in ? iy : 0)) * W + (in ? ix : 0)) * C);
+    for (int c = lane; c < q4; c += 32) {
+        uint32_t hv = 0u, lv = 0x80808080u;
+        if (in) {
+            const int4 v = __ldg(x + c);
+            if (ee <= 15) quant_pack4_e15(v.x, v.y, v.z, v.w, qh, ee, hv, lv);
+            else quant_pack4(v.x, v.y, v.z, v.w, qs1, qr, qr, hv, lv);
+        }
+        h[k0 + c] = hv; l[k0 + c] = lv;
+    }
+    for (int c4 = k0 + q4 + lane; c4 < kend; c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
+}
+
 // ---------------------------------------------------------------- GroupNorm (src/kernels.cu:173-221,285-305,420-487)
 // Per-(sample, group) accumulation record = vela_gnstat {sum, mn, mx, mean, e, ss, sd}: zeroed, then the two
 // statistics passes accumulate into it with atomics, then the finish kernel derives mean, e and sd.
@@ -674,7 +713,11 @@ void pixmax(cudaStream_t st, const int32_t* X, int rows, int C, uint32_t* pm) {
 void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H, int W, int C, int stride, int8_t* hi, int8_t* lo, int32_t* e, int Kp) {
     VELA_REQUIRE(X && pm && hi && lo && e && Kp >= 9 * C && stride >= 1, "im2col3: bad arguments");
     const int Ho = (H - 1) / stride + 1, Wo = (W - 1) / stride + 1, rows = B * Ho * Wo, Mpad = (rows + 31) / 32 * 32;
-    im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+    if (C % 4 == 0 && Kp % 4 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (reinterpret_cast<uintptr_t>(hi) & 3) == 0 &&
+        (reinterpret_cast<uintptr_t>(lo) & 3) == 0)
+        im2col3_q4_kernel<<<ceil_div(Mpad * 9, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+    else
+        im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
 }
 // statistics: accumulate sum/min/max, then the squared deviations, then mean/e/sd per (sample, group)
 void gn_stats(cudaStream_t st, const int32_t* X, int B, int T, int C, i64 den, vela_gnstat* gs) {
