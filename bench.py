@@ -334,8 +334,9 @@ class GemmCase:
 class GnConvCase:
     """Config 3: GroupNorm (32 groups) + SiLU of int32 NHWC [8, H*W, C] (uniform over the int16 range), pixel max,
     then the 3x3 conv C -> C with int8 weights the way the engine runs it, given the engine's 64 MiB split-K
-    workspace: at 320 / 640 channels the implicit conv (3x3 window exponents, windows quantised on load); at 1280
-    channels (16x16 and 8x8) the explicit im2col into hi / lo planes (window exponents included) and the planar GEMM.
+    workspace: at 320 channels (64x64) the implicit conv (3x3 window exponents, windows quantised on load); at 640
+    and 1280 channels (32x32 and below) the explicit im2col into hi / lo planes (window exponents included) and the
+    planar GEMM.
     Levels 0-2 are the configuration's shapes; level 3 (1280 ch at 8x8, the UNet's deepest level) is the shape where
     the GEMM splits K and runs the split-K reduction.  The implicit form is also timed at every level."""
     LEVELS = [(64, 320), (32, 640), (16, 1280), (8, 1280)]
@@ -369,8 +370,8 @@ class GnConvCase:
         E = abi.AEpi(); E.epi = abi.EPI_PLAIN; E.Y = self.out.data_ptr(); E.ldy = N
         E.workspace = self.ws.data_ptr(); E.workspace_bytes = 64 << 20
         self.a, self.E, self.dims = a, E, (B, Hh, C, T, N, K)
-        # the engine's rule (explicit_im2col in engine.cu): 1280 output channels on at most 16 x 16 pixels
-        self.explicit = N >= 1280 and T <= 256
+        # the engine's rule (explicit_im2col in engine.cu): 640 or more output channels on at most 32 x 32 pixels
+        self.explicit = N >= 640 and T <= 1024
         if self.explicit:
             Mp = (B * T + 63) // 64 * 64
             self.hi = torch.empty((Mp, K), dtype=torch.int8, device=device); self.lo = torch.empty_like(self.hi)

@@ -144,12 +144,14 @@ def test_conv_320ch_16x16():
         assert np.array_equal(got, exp), stride
 
 
-@pytest.mark.parametrize("B,Hh,C,N,stride,Kp", [(8, 16, 256, 1280, 1, 2304), (4, 16, 128, 1280, 2, 1216)])
+@pytest.mark.parametrize("B,Hh,C,N,stride,Kp", [(8, 16, 256, 1280, 1, 2304), (8, 16, 256, 1536, 1, 2304),
+                                                 (4, 16, 128, 1280, 2, 1216)])
 def test_conv_explicit_im2col_deep(B, Hh, C, N, stride, Kp):
-    """the engine's deep-level convolution (1280 output channels at 16x16 and below): the window-quantised im2col
-    planes (one warp per row and tap) against the oracle's im2col; then the planar GEMM at deep K (36 / 19 k-blocks,
-    where the planner weighs 256-column tiles) -- the first 128 rows against the oracle's GEMM, every row against the
-    implicit conv of the same image"""
+    """the engine's deep-level convolution (640 or more output channels at 32x32 and below): the window-quantised
+    im2col planes (one warp per row and tap) against the oracle's im2col; then the planar GEMM -- at deep K (36
+    k-blocks) on 160-column tiles (N 1280: 128 tiles in one wave) and 256-column tiles (N 1536: 96 tiles, where 160
+    columns would need two waves), at 19 k-blocks on the short-K tiles -- the first 128 rows against the oracle's
+    GEMM, every row against the implicit conv of the same image"""
     rng = np.random.default_rng(7 + stride); d = Dev()
     X = rbits(rng, (B, Hh, Hh, C), 22)
     Ho = (Hh - 1) // stride + 1; rows = B * Ho * Ho; Mp = (rows + 63) // 64 * 64

@@ -8,8 +8,8 @@
 // src/engine.cu:491-574, the step and its pipeline :599-677 (forwardIO, graph per slot, submit / collect / run).
 // Differences by design:
 //   - every GEMM, convolution and attention runs on the tcgen05 kernels; no cuBLASLt, no score buffers;
-//     3x3 convolutions quantise their windows while loading them (implicit GEMM), except the 1280-channel ones at
-//     16x16 and below, which quantise each window once into an im2col buffer for the planar GEMM;
+//     3x3 convolutions quantise their windows while loading them (implicit GEMM), except the ones with 640 or more
+//     output channels at 32x32 and below, which quantise each window once into an im2col buffer for the planar GEMM;
 //   - weights are prepared once at load: 3x3 kernels permuted to tap-major K, N padded to 64,
 //     K to 16, q|k|v and the GEGLU a|g rows merged (a|g interleaved) exactly as the reference does;
 //   - the text encoder computes only the 77 real rows (every op on that path is row-local and the
@@ -614,10 +614,10 @@ private:
         vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_X32; A.x = xd; A.ldx = K; A.rowmax = rm; A.K = L.K;
         gemm_w8a16(st_, A, int(align_up(rows, 64)), rows, L.w, L.Kp, L.Np, L.N, L.Kp, L.cst, E, lo_);
     }
-    // Which 3x3 convolutions run as explicit im2col + planar GEMM: 1280 output channels on at most 16 x 16 pixels.
-    // Measured at batch 8 (explicit vs implicit): 0.097 vs 0.124 ms at 16x16, 0.046 vs 0.060 ms at 8x8; at 32x32
-    // with 640 channels the two tie and at 64x64 the 189 MB of planes would not stay in L2.
-    static bool explicit_im2col(const Lin& L, int out_pixels) { return L.N >= 1280 && out_pixels <= 256; }
+    // Which 3x3 convolutions run as explicit im2col + planar GEMM: at least 640 output channels on at most 32 x 32
+    // pixels, where the implicit form would re-quantise each window for four or more column tiles.  At 64 x 64 with
+    // 320 channels (two column tiles) the implicit conv is faster.
+    static bool explicit_im2col(const Lin& L, int out_pixels) { return L.N >= 640 && out_pixels <= 1024; }
     // 3x3 pad-1 convolution (Engine::conv3, src/engine.cu:254-280): implicit GEMM on the int32 image
     Tensor conv3(const Tensor& x, int H, int W, const Lin& L, int stride, int32_t* out = nullptr, const int32_t* residual = nullptr, const uint32_t* pmIn = nullptr) {
         VELA_REQUIRE(L.conv3 && x.C * 9 == L.K, "conv3: shape mismatch");
@@ -629,9 +629,8 @@ private:
         const int Mp = int(align_up(rows, 64));
         int32_t* e = static_cast<int32_t*>(arena_.alloc(size_t(Mp) * 4));
         if (explicit_im2col(L, Ho * Wo) && x.C % 4 == 0) {
-            // the deep levels (1280 output channels at 16x16 and below): every window quantised once into hi / lo
-            // planes (the reference's engine takes its im2col path here too), then the planar GEMM with wide tiles;
-            // the implicit form would re-quantise each window for every one of its eight column tiles
+            // the deep levels: every window quantised once into hi / lo planes (the reference's engine takes its
+            // im2col path here too), then the planar GEMM with wide tiles
             int8_t* hi = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp)); int8_t* lo = static_cast<int8_t*>(arena_.alloc(size_t(Mp) * L.Kp));
             im2col3(st_, x.d, pm, x.B, H, W, x.C, stride, hi, lo, e, L.Kp);
             vela_asrc A; std::memset(&A, 0, sizeof(A)); A.src = VELA_SRC_I8; A.hi = hi; A.lo = lo; A.ld8 = L.Kp; A.e = e;

@@ -45,7 +45,7 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 
 // the instantiations live in gemm_inst_*.cu
 #define VELA_PERSIST_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm_persist<BN, ST, SRC, EPI>(const GemmArgs&, cudaStream_t);
-VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 4, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
+VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(160, 4, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 4, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
 VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_SPLIT3) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_QKV)
 #define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 4, SRC, EPI_PLAIN) \
     VELA_PERSIST_EXTERN(160, 4, SRC, EPI_PLAIN)
@@ -73,8 +73,9 @@ struct Plan { int bn, splits; };
 // Planar sources with deep K (>= 32 k-blocks, where the epilogue is rare) are bound by the operands' flow into shared
 // memory instead: ~40 bytes per SM clock measured whatever the tile width, against 512 clocks of MMAs per k-block (two
 // planes x two K steps of 32, each B operand fetched once for both planes) -- per k-block max(512, (2 x 128 + BN) x 64
-// / 40) clocks = 1.5 / 1.8 / 2.4 units at BN = 64 / 128 / 256.  256-column tiles keep a single accumulator buffer
-// (the epilogue does not overlap the next tile's MMAs) and are taken only when every unit runs in one wave.
+// / 40) clocks = 1.5 / 1.8 / 1.95 / 2.4 units at BN = 64 / 128 / 160 / 256.  160- and 256-column tiles keep a single
+// accumulator buffer (the epilogue does not overlap the next tile's MMAs): 160 is weighed for deep K only, 256 only
+// when every unit runs in one wave.
 Plan plan(int src, int epi, int Mp, int Mreal, int Np, int Nreal, int nkb, size_t workspace, int sms) {
     if (epi != EPI_PLAIN) return {128, 1};
     const bool reg = src != VELA_SRC_I8, deep = !reg && nkb >= 32;
@@ -82,9 +83,9 @@ Plan plan(int src, int epi, int Mp, int Mreal, int Np, int Nreal, int nkb, size_
     const int nM = ceil_div(Mp, 128);
     Plan best{reg ? 128 : 64, 1};
     double best_t = 1e30;
-    const int nb = reg ? 3 : (deep ? 3 : 2);
-    const int i8_bns[3] = {64, 128, 256};
-    const double deep_cost[3] = {1.5, 1.8, 2.4};
+    const int nb = reg ? 3 : (deep ? 4 : 2);
+    const int i8_bns[4] = {64, 128, 160, 256};
+    const double deep_cost[4] = {1.5, 1.8, 1.95, 2.4};
     for (int i = 0; i < nb; ++i) {
         const int bn = reg ? REG_BNS[i] : i8_bns[i];
         if (!reg && bn == 128 && Nreal % 128 != 0 && Nreal > 128) continue;
@@ -189,6 +190,7 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
     if (epi == EPI_PLAIN) {
         if (src == VELA_SRC_I8) {
             if (BN == 256) launch_gemm_persist<256, 4, SRC_I8, EPI_PLAIN>(a, st);
+            else if (BN == 160) launch_gemm_persist<160, 4, SRC_I8, EPI_PLAIN>(a, st);
             else if (BN == 128) launch_gemm_persist<128, 6, SRC_I8, EPI_PLAIN>(a, st);
             else launch_gemm_persist<64, 6, SRC_I8, EPI_PLAIN>(a, st);
         }

@@ -32,9 +32,10 @@ template <int BN, int STAGES, int SRC, int EPI> struct PersistCfg {
     static constexpr int TCOLS = ACC_BUFS * ACC_COLS;
     static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : (TCOLS <= 64 ? 64 : (TCOLS <= 128 ? 128 : (TCOLS <= 256 ? 256 : 512)));
     static constexpr int NCW = REG ? 8 : 0;
-    // epilogue warps: 16 (four per TMEM lane quarter) for planar sources, 8 where converters share the SM or a
-    // q|k|v head (64 columns) is one thread's unit
-    static constexpr int EW = (REG || EPI == EPI_QKV) ? 8 : 16;
+    // epilogue warps: 16 (four per TMEM lane quarter) for planar sources, 8 where converters share the SM, a
+    // q|k|v head (64 columns) is one thread's unit, or the tile width is not a multiple of 64 (160 columns: each
+    // thread takes 80, a multiple of the 16-column loads)
+    static constexpr int EW = (REG || EPI == EPI_QKV || BN % 64 != 0) ? 8 : 16;
     // with two accumulator buffers and 16 epilogue warps, two groups of 8 take alternate tiles (group g drains
     // buffer g), so the latency chains of two tiles' epilogues (constants, residual, TMEM loads, stores) overlap
     // (the GEGLU and split epilogues; the plain one measured faster with all 16 warps on every tile)

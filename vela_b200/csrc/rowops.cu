@@ -132,7 +132,8 @@ __global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restr
 
 // The same for C % 4 == 0 and Kp % 4 == 0: one warp per (output row, tap), four channels per lane and step (a
 // 16-byte load, four hi and four lo bytes stored as words); the row's window exponent from the nine pixel maxima
-// (a warp max), written by the tap-0 warp; the tap-8 warp also fills the K padding [9C, Kp).
+// (a warp max), written by the tap-0 warp; the tap-8 warp also fills the K padding [9C, Kp).  Latency-bound (one
+// short chain of loads per warp), so the loads are batched ahead of the arithmetic.
 __global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __restrict__ pm, int B, int H, int W, int C, int stride, int Ho,
                                   int Wo, int rows, int Mpad, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
     const int lane = threadIdx.x & 31, wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -146,25 +147,41 @@ __global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __re
         return;
     }
     const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
+    const int iy = oy * stride - 1 + tap / 3, ix = ox * stride - 1 + tap % 3;
+    const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+    const int4* x = reinterpret_cast<const int4*>(X + ((size_t(b) * H + (in ? iy : 0)) * W + (in ? ix : 0)) * C);
+    // the first eight 16-byte loads of this lane go out before the window exponent is formed (they do not depend on
+    // it); a padding tap quantises zeros (hi 0, lo 0x80)
+    int4 v[8];
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = in && lane + 32 * j < q4 ? __ldg(x + lane + 32 * j) : make_int4(0, 0, 0, 0);
     u32 m = 0;
     if (lane < 9) {
-        const int iy = oy * stride - 1 + lane / 3, ix = ox * stride - 1 + lane % 3;
-        if (iy >= 0 && iy < H && ix >= 0 && ix < W) m = __ldg(pm + (size_t(b) * H + iy) * W + ix);
+        const int py = oy * stride - 1 + lane / 3, px = ox * stride - 1 + lane % 3;
+        if (py >= 0 && py < H && px >= 0 && px < W) m = __ldg(pm + (size_t(b) * H + py) * W + px);
     }
     const int ee = row_exp(__reduce_max_sync(0xffffffffu, m));
     if (tap == 0 && lane == 0) e[r] = ee;
     const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
-    const int iy = oy * stride - 1 + tap / 3, ix = ox * stride - 1 + tap % 3;
-    const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
-    const int4* x = reinterpret_cast<const int4*>(X + ((size_t(b) * H + (in ? iy : 0)) * W + (in ? ix : 0)) * C);
-    for (int c = lane; c < q4; c += 32) {
-        uint32_t hv = 0u, lv = 0x80808080u;
-        if (in) {
-            const int4 v = __ldg(x + c);
-            if (ee <= 15) quant_pack4_e15(v.x, v.y, v.z, v.w, qh, ee, hv, lv);
-            else quant_pack4(v.x, v.y, v.z, v.w, qs1, qr, qr, hv, lv);
-        }
+    auto put = [&](const int4& w, int c) {
+        uint32_t hv, lv;
+        if (ee <= 15) quant_pack4_e15(w.x, w.y, w.z, w.w, qh, ee, hv, lv);
+        else quant_pack4(w.x, w.y, w.z, w.w, qs1, qr, qr, hv, lv);
         h[k0 + c] = hv; l[k0 + c] = lv;
+    };
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if (lane + 32 * j >= q4) break;
+        put(v[j], lane + 32 * j);
+    }
+    for (int c0 = lane + 256; c0 < q4; c0 += 128) {
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = in && c0 + 32 * j < q4 ? __ldg(x + c0 + 32 * j) : make_int4(0, 0, 0, 0);
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (c0 + 32 * j >= q4) break;
+            put(v[j], c0 + 32 * j);
+        }
     }
     for (int c4 = k0 + q4 + lane; c4 < kend; c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
 }
