@@ -45,7 +45,7 @@ __global__ void gemm_splitk_reduce(const int32_t* __restrict__ partial, int spli
 
 // the instantiations live in gemm_inst_*.cu
 #define VELA_PERSIST_EXTERN(BN, ST, SRC, EPI) extern template void launch_gemm_persist<BN, ST, SRC, EPI>(const GemmArgs&, cudaStream_t);
-VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(160, 4, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 4, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
+VELA_PERSIST_EXTERN(64, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(160, 6, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(256, 5, SRC_I8, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_GEGLU)
 VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_SPLIT3) VELA_PERSIST_EXTERN(128, 6, SRC_I8, EPI_QKV)
 #define VELA_PERSIST_REG(SRC) VELA_PERSIST_EXTERN(64, 4, SRC, EPI_PLAIN) VELA_PERSIST_EXTERN(128, 4, SRC, EPI_PLAIN) \
     VELA_PERSIST_EXTERN(160, 4, SRC, EPI_PLAIN)
@@ -189,8 +189,8 @@ void gemm_w8a16(cudaStream_t st, const vela_asrc& A, int Mp, int Mreal, const in
 
     if (epi == EPI_PLAIN) {
         if (src == VELA_SRC_I8) {
-            if (BN == 256) launch_gemm_persist<256, 4, SRC_I8, EPI_PLAIN>(a, st);
-            else if (BN == 160) launch_gemm_persist<160, 4, SRC_I8, EPI_PLAIN>(a, st);
+            if (BN == 256) launch_gemm_persist<256, 5, SRC_I8, EPI_PLAIN>(a, st);
+            else if (BN == 160) launch_gemm_persist<160, 6, SRC_I8, EPI_PLAIN>(a, st);
             else if (BN == 128) launch_gemm_persist<128, 6, SRC_I8, EPI_PLAIN>(a, st);
             else launch_gemm_persist<64, 6, SRC_I8, EPI_PLAIN>(a, st);
         }

@@ -130,60 +130,69 @@ __global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restr
     pad_cols(h, l, K, Kp, lane);
 }
 
-// The same for C % 4 == 0 and Kp % 4 == 0: one warp per (output row, tap), four channels per lane and step (a
-// 16-byte load, four hi and four lo bytes stored as words); the row's window exponent from the nine pixel maxima
-// (a warp max), written by the tap-0 warp; the tap-8 warp also fills the K padding [9C, Kp).  Latency-bound (one
-// short chain of loads per warp), so the loads are batched ahead of the arithmetic.
+// The same for C % 4 == 0 and Kp % 4 == 0: four channels per lane and step (a 16-byte load, four hi and four lo
+// bytes stored as words).  ALL_TAPS: one warp per output row, the nine taps in turn (large images: the row's setup
+// and window exponent are paid once); else one warp per (row, tap) (small images: nine times the warps to fill the
+// SMs).  The window exponent comes from the nine pixel maxima (a warp max) while the warp's first loads are in
+// flight, and is written by the warp of tap 0; the warp of tap 8 fills the K padding [9C, Kp).  Up to eight 16-byte
+// loads per lane are issued before any of them is quantised.
+template <bool ALL_TAPS>
 __global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __restrict__ pm, int B, int H, int W, int C, int stride, int Ho,
                                   int Wo, int rows, int Mpad, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
     const int lane = threadIdx.x & 31, wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int r = wg / 9, tap = wg - r * 9;
+    const int r = ALL_TAPS ? wg : wg / 9, t0 = ALL_TAPS ? 0 : wg - r * 9, t1 = ALL_TAPS ? 9 : t0 + 1;
     if (r >= Mpad) return;
     u32* h = reinterpret_cast<u32*>(hi + size_t(r) * Kp);
     u32* l = reinterpret_cast<u32*>(lo + size_t(r) * Kp);
-    const int q4 = C >> 2, k0 = tap * q4, kend = tap == 8 ? (Kp >> 2) : k0 + q4;
+    const int q4 = C >> 2, kq = 9 * q4;
     if (r >= rows) {
-        for (int c4 = k0 + lane; c4 < kend; c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
+        for (int c4 = t0 * q4 + lane; c4 < (t1 == 9 ? (Kp >> 2) : t1 * q4); c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
         return;
     }
     const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
-    const int iy = oy * stride - 1 + tap / 3, ix = ox * stride - 1 + tap % 3;
-    const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
-    const int4* x = reinterpret_cast<const int4*>(X + ((size_t(b) * H + (in ? iy : 0)) * W + (in ? ix : 0)) * C);
-    // the first eight 16-byte loads of this lane go out before the window exponent is formed (they do not depend on
-    // it); a padding tap quantises zeros (hi 0, lo 0x80)
+    const int4* img = reinterpret_cast<const int4*>(X + size_t(b) * H * W * C);
+    // 16-byte group c of tap t (zeros where the tap falls on the padding)
+    auto tap_ptr = [&](int t, bool& in) {
+        const int iy = oy * stride - 1 + t / 3, ix = ox * stride - 1 + t % 3;
+        in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+        return img + (size_t(in ? iy : 0) * W + (in ? ix : 0)) * q4;
+    };
+    // the first tap's first loads, then the exponent (every lane takes part in the warp max, whatever C)
     int4 v[8];
+    bool in;
+    const int4* x = tap_ptr(t0, in);
     #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = in && lane + 32 * j < q4 ? __ldg(x + lane + 32 * j) : make_int4(0, 0, 0, 0);
     u32 m = 0;
     if (lane < 9) {
+        bool pin;
+        tap_ptr(lane, pin);
         const int py = oy * stride - 1 + lane / 3, px = ox * stride - 1 + lane % 3;
-        if (py >= 0 && py < H && px >= 0 && px < W) m = __ldg(pm + (size_t(b) * H + py) * W + px);
+        if (pin) m = __ldg(pm + (size_t(b) * H + py) * W + px);
     }
     const int ee = row_exp(__reduce_max_sync(0xffffffffu, m));
-    if (tap == 0 && lane == 0) e[r] = ee;
+    if (t0 == 0 && lane == 0) e[r] = ee;
     const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
-    auto put = [&](const int4& w, int c) {
-        uint32_t hv, lv;
-        if (ee <= 15) quant_pack4_e15(w.x, w.y, w.z, w.w, qh, ee, hv, lv);
-        else quant_pack4(w.x, w.y, w.z, w.w, qs1, qr, qr, hv, lv);
-        h[k0 + c] = hv; l[k0 + c] = lv;
-    };
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        if (lane + 32 * j >= q4) break;
-        put(v[j], lane + 32 * j);
-    }
-    for (int c0 = lane + 256; c0 < q4; c0 += 128) {
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = in && c0 + 32 * j < q4 ? __ldg(x + c0 + 32 * j) : make_int4(0, 0, 0, 0);
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (c0 + 32 * j >= q4) break;
-            put(v[j], c0 + 32 * j);
+    for (int t = t0; t < t1; ++t) {
+        if (t > t0) x = tap_ptr(t, in);
+        for (int c0 = lane; c0 < q4; c0 += 256) {
+            if (t > t0 || c0 != lane) {
+                #pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = in && c0 + 32 * j < q4 ? __ldg(x + c0 + 32 * j) : make_int4(0, 0, 0, 0);
+            }
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + 32 * j;
+                if (c >= q4) break;
+                uint32_t hv, lv;
+                if (ee <= 15) quant_pack4_e15(v[j].x, v[j].y, v[j].z, v[j].w, qh, ee, hv, lv);
+                else quant_pack4(v[j].x, v[j].y, v[j].z, v[j].w, qs1, qr, qr, hv, lv);
+                h[t * q4 + c] = hv; l[t * q4 + c] = lv;
+            }
         }
     }
-    for (int c4 = k0 + q4 + lane; c4 < kend; c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
+    if (t1 == 9)
+        for (int c4 = kq + lane; c4 < (Kp >> 2); c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
 }
 
 // ---------------------------------------------------------------- GroupNorm (src/kernels.cu:173-221,285-305,420-487)
@@ -732,7 +741,13 @@ void im2col3(cudaStream_t st, const int32_t* X, const uint32_t* pm, int B, int H
     const int Ho = (H - 1) / stride + 1, Wo = (W - 1) / stride + 1, rows = B * Ho * Wo, Mpad = (rows + 31) / 32 * 32;
     if (C % 4 == 0 && Kp % 4 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (reinterpret_cast<uintptr_t>(hi) & 3) == 0 &&
         (reinterpret_cast<uintptr_t>(lo) & 3) == 0)
-        im2col3_q4_kernel<<<ceil_div(Mpad * 9, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+    {
+        // whole rows per warp once the rows alone give every SM about 32 warps
+        if (Mpad >= 32 * sm_count())
+            im2col3_q4_kernel<true><<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+        else
+            im2col3_q4_kernel<false><<<ceil_div(Mpad * 9, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
+    }
     else
         im2col3_kernel<<<ceil_div(Mpad, 8), 256, 0, st>>>(X, pm, B, H, W, C, stride, Ho, Wo, rows, Mpad, hi, lo, e, Kp);
 }
