@@ -6,6 +6,8 @@ kernel computes and checks it against the spec form on edge values and seeded ra
 - quant_pack4 (intops.cuh): q = ((v >> s1) + r) >> s2, then cvt.pack.sat.s16.s32 and max.s16x2 with -32767, split
   into hi / lo bytes  ==  quant16(v, e) = clamp(rshr(v, e), +-32767) split into planes;
 - quant_pack4_e15: (v + 2^(e-1)) >> e for e <= 15 and |v| < 2^(15+e)  ==  rshr(v, e);
+- quant_nosat / quant_pack4_e15_nosat: for a row maximum m with m + 2^(e-1) < 2^(15+e) (or e = 0) no value of the
+  row saturates, and four byte selections of the 32-bit results give the hi / lo plane bytes;
 - the q|k|v / V plane sums: sum q = 256 sum hi + sum lo + 128 n;
 - lut16_s (intops.cuh): the sentinel table indexed by clamp((x >> 10) + 1024, -1, 2048) + 1  ==  lut16;
 - lut_act_s: x * lut / 2^16 rounded needs no saturation when 0 <= lut <= 65536;
@@ -74,6 +76,49 @@ def test_two_operation_rounding_below_e16():
             assert abs(v + h) < 2**31
             q = max(pack_sat16((v + h) >> e), -32767)
             assert q == quant16(v, e), (e, v)
+
+
+def byte_perm(x, y, sel):
+    b = (x & 0xFFFFFFFF).to_bytes(4, "little") + (y & 0xFFFFFFFF).to_bytes(4, "little")
+    return int.from_bytes(bytes(b[(sel >> (4 * i)) & 7] for i in range(4)), "little")
+
+
+def quant_nosat(m, e):
+    return e == 0 or m + (1 << (e - 1)) < (1 << (15 + e))
+
+
+def test_no_saturation_rows():
+    # quant_nosat(m, e) with e = row_exp(m) holds exactly when no v in [-m, m] saturates (the extremes decide,
+    # rshr being monotone); when it fails, v = m does saturate
+    rnd = random.Random(15)
+    ms = [0, 1, 32767, 32768, 65535, 65536, 2**31 - 1, 2**32 - 1]
+    for e in range(1, 18):
+        top = (1 << (15 + e)) - 1
+        ms += [top, top - (1 << (e - 1)), top - (1 << (e - 1)) + 1, 1 << (14 + e), (1 << (14 + e)) + 1]
+    ms += [rnd.randint(0, 2**32 - 1) >> rnd.randint(0, 31) for _ in range(20000)]
+    for m in ms:
+        e = row_exp(m)
+        if m >= 2**31:
+            continue                      # int32 activations: |v| <= 2^31
+        free = -32767 <= rshr(-m, e) and rshr(m, e) <= 32767
+        assert quant_nosat(m, e) == free, (m, e)
+        if not free:
+            assert quant16(m, e) != rshr(m, e)
+
+
+def test_nosat_byte_packing():
+    rnd = random.Random(16)
+    for _ in range(20000):
+        q = [rnd.randint(-32767, 32767) for _ in range(4)]
+        if rnd.random() < 0.1:
+            q = [rnd.choice([-32767, 32767, 0, -1, 255, -256]) for _ in range(4)]
+        a, b = byte_perm(q[0], q[1], 0x4051), byte_perm(q[2], q[3], 0x4051)
+        hw, lw = byte_perm(a, b, 0x5410), byte_perm(a, b, 0x7632) ^ 0x80808080
+        his = [(hw >> (8 * i)) & 255 for i in range(4)]
+        los = [(lw >> (8 * i)) & 255 for i in range(4)]
+        for i in range(4):
+            h, l = planes(q[i])
+            assert his[i] == h & 255 and los[i] == l & 255, (q, i)
 
 
 def test_row_exponent_bounds_the_row():

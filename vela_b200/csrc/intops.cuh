@@ -82,6 +82,20 @@ __device__ __forceinline__ void quant_pack4_e15(int v0, int v1, int v2, int v3, 
     hw = __byte_perm(w01, w23, 0x7531);
     lw = __byte_perm(w01, w23, 0x6420) ^ 0x80808080u;
 }
+// Whether a row whose largest magnitude is m (e = row_exp(m)) needs the +-32767 saturation at all: for e = 0 every
+// |v| <= m < 2^15; for e >= 1 the rounded extremes (m + 2^(e-1)) >> e and (-m + 2^(e-1)) >> e stay inside +-32767
+// exactly when m + 2^(e-1) < 2^(15+e).  Most rows qualify (only an m in the top 2^(e-1) of its binade does not).
+__device__ __forceinline__ bool quant_nosat(u32 m, int e) {
+    return e == 0 || uint64_t(m) + (uint64_t(1) << (e - 1)) < (uint64_t(1) << (15 + e));
+}
+// quant_pack4_e15 for such a row: the rounded values are 16-bit already, so their hi / lo plane bytes are bytes 1
+// and 0 of the 32-bit results, gathered by four byte selections (lo bytes then offset by 128).
+__device__ __forceinline__ void quant_pack4_e15_nosat(int v0, int v1, int v2, int v3, int h, int e, uint32_t& hw, uint32_t& lw) {
+    const int q0 = (v0 + h) >> e, q1 = (v1 + h) >> e, q2 = (v2 + h) >> e, q3 = (v3 + h) >> e;
+    const uint32_t a = __byte_perm(q0, q1, 0x4051), b = __byte_perm(q2, q3, 0x4051);   // [q0.b1 q1.b1 q0.b0 q1.b0] ...
+    hw = __byte_perm(a, b, 0x5410);
+    lw = __byte_perm(a, b, 0x7632) ^ 0x80808080u;
+}
 // hi bytes / lo bytes of four 16-bit values packed into one word each
 __device__ __forceinline__ u32 pack_hi4(int q0, int q1, int q2, int q3) {
     return __byte_perm(__byte_perm(q0, q1, 0x0051), __byte_perm(q2, q3, 0x0051), 0x5410);

@@ -130,12 +130,39 @@ __global__ void im2col3_kernel(const int32_t* __restrict__ X, const u32* __restr
     pad_cols(h, l, K, Kp, lane);
 }
 
-// The same for C % 4 == 0 and Kp % 4 == 0: four channels per lane and step (a 16-byte load, four hi and four lo
-// bytes stored as words).  ALL_TAPS: one warp per output row, the nine taps in turn (large images: the row's setup
-// and window exponent are paid once); else one warp per (row, tap) (small images: nine times the warps to fill the
-// SMs).  The window exponent comes from the nine pixel maxima (a warp max) while the warp's first loads are in
-// flight, and is written by the warp of tap 0; the warp of tap 8 fills the K padding [9C, Kp).  Up to eight 16-byte
-// loads per lane are issued before any of them is quantised.
+// One tap of one im2col row: its C / 4 16-byte groups quantised with the row's exponent into four hi and four lo
+// bytes each.  Full-warp steps (two loads in flight) carry no predicate, the last partial step one; a tap on the
+// padding (warp-uniform) writes the zero value (hi 0, lo 0x80).
+// Q: 0 = exponent <= 15 and no saturation possible (quant_nosat), 1 = exponent <= 15, 2 = any exponent.
+template <int Q>
+__device__ __forceinline__ void im2col_tap(const int4* __restrict__ x, bool in, u32* __restrict__ hp, u32* __restrict__ lp, int q4, int lane,
+                                           int qa, int qb) {
+    auto put = [&](const int4& v, int c) {
+        uint32_t hv, lv;
+        if constexpr (Q == 0) quant_pack4_e15_nosat(v.x, v.y, v.z, v.w, qa, qb, hv, lv);
+        else if constexpr (Q == 1) quant_pack4_e15(v.x, v.y, v.z, v.w, qa, qb, hv, lv);
+        else quant_pack4(v.x, v.y, v.z, v.w, qa, qb, qb, hv, lv);
+        hp[c] = hv; lp[c] = lv;
+    };
+    if (!in) {
+        for (int c = lane; c < q4; c += 32) { hp[c] = 0u; lp[c] = 0x80808080u; }
+        return;
+    }
+    const int nfull = q4 >> 5;
+    int c = lane;
+    for (int j = 0; j + 2 <= nfull; j += 2, c += 64) {
+        const int4 v0 = __ldg(x + c), v1 = __ldg(x + c + 32);
+        put(v0, c); put(v1, c + 32);
+    }
+    if (nfull & 1) { put(__ldg(x + c), c); c += 32; }
+    if (c < q4) put(__ldg(x + c), c);
+}
+
+// The same for C % 4 == 0 and Kp % 4 == 0.  ALL_TAPS: one warp per output row, the nine taps in turn (large images:
+// the row's setup and window exponent are paid once); else one warp per (row, tap) (small images: nine times the
+// warps to fill the SMs).  The window exponent comes from the nine pixel maxima (a warp max), written by the warp of
+// tap 0; the warp of tap 8 fills the K padding [9C, Kp).  The quantisation form is chosen once per row: without the
+// saturation when the window maximum rules it out (quant_nosat), the common case.
 template <bool ALL_TAPS>
 __global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __restrict__ pm, int B, int H, int W, int C, int stride, int Ho,
                                   int Wo, int rows, int Mpad, int8_t* __restrict__ hi, int8_t* __restrict__ lo, int32_t* __restrict__ e, int Kp) {
@@ -151,45 +178,22 @@ __global__ void im2col3_q4_kernel(const int32_t* __restrict__ X, const u32* __re
     }
     const int hw = Ho * Wo, b = r / hw, p = r - b * hw, oy = p / Wo, ox = p - oy * Wo;
     const int4* img = reinterpret_cast<const int4*>(X + size_t(b) * H * W * C);
-    // 16-byte group c of tap t (zeros where the tap falls on the padding)
-    auto tap_ptr = [&](int t, bool& in) {
-        const int iy = oy * stride - 1 + t / 3, ix = ox * stride - 1 + t % 3;
-        in = iy >= 0 && iy < H && ix >= 0 && ix < W;
-        return img + (size_t(in ? iy : 0) * W + (in ? ix : 0)) * q4;
-    };
-    // the first tap's first loads, then the exponent (every lane takes part in the warp max, whatever C)
-    int4 v[8];
-    bool in;
-    const int4* x = tap_ptr(t0, in);
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = in && lane + 32 * j < q4 ? __ldg(x + lane + 32 * j) : make_int4(0, 0, 0, 0);
     u32 m = 0;
     if (lane < 9) {
-        bool pin;
-        tap_ptr(lane, pin);
         const int py = oy * stride - 1 + lane / 3, px = ox * stride - 1 + lane % 3;
-        if (pin) m = __ldg(pm + (size_t(b) * H + py) * W + px);
+        if (py >= 0 && py < H && px >= 0 && px < W) m = __ldg(pm + (size_t(b) * H + py) * W + px);
     }
-    const int ee = row_exp(__reduce_max_sync(0xffffffffu, m));
+    const u32 wm = __reduce_max_sync(0xffffffffu, m);
+    const int ee = row_exp(wm);
     if (t0 == 0 && lane == 0) e[r] = ee;
-    const int qs1 = ee > 0 ? ee - 1 : 0, qr = ee > 0 ? 1 : 0, qh = (1 << ee) >> 1;
+    const int qf = ee > 15 ? 2 : (quant_nosat(wm, ee) ? 0 : 1);       // warp-uniform
     for (int t = t0; t < t1; ++t) {
-        if (t > t0) x = tap_ptr(t, in);
-        for (int c0 = lane; c0 < q4; c0 += 256) {
-            if (t > t0 || c0 != lane) {
-                #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = in && c0 + 32 * j < q4 ? __ldg(x + c0 + 32 * j) : make_int4(0, 0, 0, 0);
-            }
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = c0 + 32 * j;
-                if (c >= q4) break;
-                uint32_t hv, lv;
-                if (ee <= 15) quant_pack4_e15(v[j].x, v[j].y, v[j].z, v[j].w, qh, ee, hv, lv);
-                else quant_pack4(v[j].x, v[j].y, v[j].z, v[j].w, qs1, qr, qr, hv, lv);
-                h[t * q4 + c] = hv; l[t * q4 + c] = lv;
-            }
-        }
+        const int iy = oy * stride - 1 + t / 3, ix = ox * stride - 1 + t % 3;
+        const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+        const int4* x = img + (size_t(in ? iy : 0) * W + (in ? ix : 0)) * q4;
+        if (qf == 0) im2col_tap<0>(x, in, h + t * q4, l + t * q4, q4, lane, (1 << ee) >> 1, ee);
+        else if (qf == 1) im2col_tap<1>(x, in, h + t * q4, l + t * q4, q4, lane, (1 << ee) >> 1, ee);
+        else im2col_tap<2>(x, in, h + t * q4, l + t * q4, q4, lane, ee - 1, 1);
     }
     if (t1 == 9)
         for (int c4 = kq + lane; c4 < (Kp >> 2); c4 += 32) { h[c4] = 0u; l[c4] = 0x80808080u; }
